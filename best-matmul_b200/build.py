@@ -1,0 +1,69 @@
+"""Build the sm_100a GEMM library (lib/libbmgemm.so) and the C++ harness.
+
+    python best-matmul_b200/build.py [--force] [--verbose]
+
+nvcc cross-compiles for sm_100a without a GPU. The library links the CUDA
+runtime statically so it does not depend on which libcudart a host process
+(e.g. PyTorch) loaded first.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+LIB_DIR = os.path.join(HERE, "lib")
+LIB = os.path.join(LIB_DIR, "libbmgemm.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xptxas", "-v",
+                     "-Xcompiler", "-fPIC", "-cudart", "static"]
+
+
+def nvcc() -> str:
+    cand = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+    return cand if os.path.exists(cand) else "nvcc"
+
+
+def _sources():
+    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC))
+            if f.endswith((".cu", ".cuh"))] + [os.path.join(ROOT, "include", "bm_gemm.h")]
+
+
+def _stale(target, sources) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(s) > t for s in sources)
+
+
+def build_library(force=False, verbose=False) -> str:
+    os.makedirs(LIB_DIR, exist_ok=True)
+    if not force and not _stale(LIB, _sources()):
+        return LIB
+    cmd = [nvcc()] + NVCC_FLAGS + ["-shared", "-o", LIB, os.path.join(CSRC, "bm_gemm.cu")]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or res.returncode != 0:
+        sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed building {LIB}")
+    with open(os.path.join(LIB_DIR, "ptxas_info.txt"), "w") as f:
+        f.write(" ".join(cmd) + "\n" + res.stderr)
+    return LIB
+
+
+def build_all(force=False, verbose=False) -> None:
+    build_library(force, verbose)
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    args = ap.parse_args()
+    build_all(args.force, args.verbose)
+    print("built", LIB)
