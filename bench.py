@@ -94,18 +94,20 @@ class ClockSampler:
         self._period = period_s
         try:
             import pynvml
+            import torch
             pynvml.nvmlInit()
-            bus = None
-            try:
-                import torch
-                bus = torch.cuda.get_device_properties(device_index).pci_bus_id
-            except Exception:
-                pass
-            if bus:
-                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode()
-                                                               if isinstance(bus, str) else bus)
-            else:
-                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            # NVML and CUDA may number devices differently: match on PCI location.
+            props = torch.cuda.get_device_properties(device_index)
+            want = (int(props.pci_domain_id), int(props.pci_bus_id), int(props.pci_device_id))
+            self._h = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                pi = pynvml.nvmlDeviceGetPciInfo(h)
+                if (int(pi.domain), int(pi.bus), int(pi.device)) == want:
+                    self._h = h
+                    break
+            if self._h is None:
+                raise RuntimeError(f"no NVML device at PCI {want}")
             self._nvml = pynvml
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
             self.ok = True
