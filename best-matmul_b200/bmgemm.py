@@ -288,3 +288,20 @@ def alloc_operands(m, n, k, layout, device="cuda", mode=4, seed=0, row0=0, total
         raise ValueError("layout must be NT or TN")
     c = torch.empty((n, m), dtype=torch.float16, device=device)
     return a, b, c
+
+
+def run_noalloc(m, n, k, layout, a_ptr, b_ptr, c_ptr, lda=0, ldb=0, ldc=0, variant=0,
+                stream=None, wait=True) -> tuple[int, int]:
+    """bm_gemm_run_noalloc: one GEMM with no device allocation (the kernel's
+    error word lives in the library's static device array). For callers that
+    cannot call cudaMalloc. The first call on a device does the per-device
+    set-up; calls that overlap on the GPU share the array and race on it.
+    Returns (status code, device error bits); wait=False returns at once."""
+    lib = load()
+    fn = lib.bm_gemm_run_noalloc
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.POINTER(GemmDesc), ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]
+    d = make_desc(m, n, k, layout, a_ptr, b_ptr, c_ptr, lda, ldb, ldc, variant)
+    bits = ctypes.c_uint32(0)
+    rc = fn(ctypes.byref(d), _stream_handle(stream), ctypes.byref(bits) if wait else None)
+    return rc, bits.value

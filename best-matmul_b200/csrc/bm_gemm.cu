@@ -220,6 +220,7 @@ const char* bm_gemm_error_string(int code) {
     case BM_ERR_DEVICE_TIMEOUT: return "a bounded wait inside the GEMM kernel expired";
     case BM_ERR_VARIANT: return "unknown kernel variant";
     case BM_ERR_TILE_DIVISIBILITY: return "selected kernel requires M % CTA_M == 0, N % CTA_N == 0, K % CTA_K == 0";
+    case BM_ERR_SCRATCH_LIMIT: return "call needs more scratch than the no-alloc entry point's static device array holds";
     default: return "unknown error";
   }
 }
@@ -437,4 +438,135 @@ extern "C" int bm_fill_fp16(void* dst, int64_t rows, int64_t cols, int64_t ld, i
   fill_fp16_kernel<<<sms * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<__half*>(dst), rows, cols, ld, row_major, row0, full_ld, mode, key, matrix_id);
   return cudaGetLastError() == cudaSuccess ? BM_OK : BM_ERR_CUDA;
+}
+
+// ------------------------------------------------------- no-alloc entry point
+// bm_gemm_run_noalloc: the same GEMM kernel, launched without any device
+// allocation, for callers that cannot call cudaMalloc (memory owned by another
+// allocator, no device allocation allowed after start-up, or no tolerance for
+// cudaMalloc/cudaFree's device-wide synchronisation).
+//
+// The kernel's scratch is its error word. Here it lives in a file-scope
+// device array instead of a cudaMalloc'd buffer. Host code must not use the
+// array's name as a device address: its device address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) on the
+// first call, and that pointer is what the kernel receives.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = BM_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocScratchBytes / sizeof(uint32_t)];
+
+// Scratch one call needs: the kernel's single 32-bit error word.
+constexpr size_t kNoAllocScratchPerCall = sizeof(uint32_t);
+
+struct NoAllocDevice {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  uint32_t* scratch = nullptr;
+};
+NoAllocDevice g_noalloc_devices[64];
+
+}  // namespace
+
+extern "C" int bm_gemm_run_noalloc(const bm_gemm_desc* d, void* stream, uint32_t* device_status) {
+  if (device_status) *device_status = 0;
+  int rc = bm_gemm_check(d);
+  if (rc != BM_OK) return rc;
+  if (kNoAllocScratchPerCall > kNoAllocScratchBytes) return BM_ERR_SCRATCH_LIMIT;
+  Resolved r;
+  resolve(d, &r);
+  const int v = pick_variant(d);
+
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return BM_ERR_CUDA;
+  if (device < 0 || device >= 64) return BM_ERR_CUDA;
+  int major = 0, minor = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return BM_ERR_CUDA;
+  if (major != 10 || minor != 0) return BM_ERR_DEVICE;
+
+  // Once per device, with that device current: device address of the array.
+  NoAllocDevice& nd = g_noalloc_devices[device];
+  std::call_once(nd.once, [&nd] {
+    void* p = nullptr;
+    nd.err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    nd.scratch = static_cast<uint32_t*>(p);
+  });
+  if (nd.err != cudaSuccess || nd.scratch == nullptr) return BM_ERR_CUDA;
+
+  // A handle-shaped parameter block on the stack (no allocation).
+  bm_gemm_handle h;
+  std::memset(&h, 0, sizeof(h));
+  h.variant = v;
+  h.nt = r.nt;
+  h.device = device;
+  h.cta_group = kVariants[v].cta_group;
+  h.tile_m = 128 * h.cta_group;
+  h.tile_n = kVariants[v].tile_n;
+  h.stages = kVariants[v].stages;
+  const int rows_b = h.tile_n / h.cta_group;
+  bool ok;
+  if (r.nt) {
+    ok = encode_2d(&h.tmap_a, d->a, d->m, d->k, r.lda, 64, 64, true) &&
+         encode_2d(&h.tmap_b, d->b, d->n, d->k, r.ldb, 64, 64, true);
+  } else {
+    ok = encode_2d(&h.tmap_a, d->a, d->k, d->m, r.lda, 64, 128, true) &&
+         encode_2d(&h.tmap_b, d->b, d->k, d->n, r.ldb, 64, static_cast<uint32_t>(rows_b), true);
+  }
+  ok = ok && encode_2d(&h.tmap_c, d->c, d->m, d->n, r.ldc, 32, 32, false);
+  if (!ok) return BM_ERR_CUDA;
+
+  int max_clusters = 0, smem = 0;
+  cudaError_t e = cudaErrorInvalidValue;
+  switch (v * 2 + (r.nt ? 1 : 0)) {
+#define BM_NOALLOC_CASE(VID, CG, BN, ST)                                               \
+  case VID * 2 + 0:                                                                    \
+    e = geometry<CG, BN, ST, false>(device, sms, VID, &max_clusters, &smem);           \
+    h.launch = &launch_variant<CG, BN, ST, false>;                                     \
+    break;                                                                             \
+  case VID * 2 + 1:                                                                    \
+    e = geometry<CG, BN, ST, true>(device, sms, VID, &max_clusters, &smem);            \
+    h.launch = &launch_variant<CG, BN, ST, true>;                                      \
+    break;
+    BM_NOALLOC_CASE(BM_VARIANT_2CTA_256x256, 2, 256, 6)
+    BM_NOALLOC_CASE(BM_VARIANT_1CTA_128x256, 1, 256, 4)
+    BM_NOALLOC_CASE(BM_VARIANT_1CTA_128x128, 1, 128, 6)
+    BM_NOALLOC_CASE(BM_VARIANT_2CTA_256x128, 2, 128, 6)
+#undef BM_NOALLOC_CASE
+    default: break;
+  }
+  if (e != cudaSuccess || max_clusters <= 0) return BM_ERR_CUDA;
+  h.smem_bytes = smem;
+
+  GemmParams& p = h.params;
+  p.m = d->m;
+  p.n = d->n;
+  p.k = d->k;
+  p.tiles_m = (d->m + h.tile_m - 1) / h.tile_m;
+  p.tiles_n = (d->n + h.tile_n - 1) / h.tile_n;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.k_blocks = (d->k + 63) / 64;
+  p.group_m = 8;
+  p.timeout_ns = kDefaultTimeoutNs;
+  p.debug = 0;
+  p.status = nd.scratch;
+  const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
+  h.grid = clusters * h.cta_group;
+
+  // The error word must start at zero; the array keeps the previous call's
+  // contents otherwise. Ordered before the kernel on the same stream.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(nd.scratch, 0, kNoAllocScratchPerCall, s) != cudaSuccess) return BM_ERR_CUDA;
+  if (h.launch(&h, s) != cudaSuccess) return BM_ERR_CUDA;
+  if (device_status) {
+    uint32_t bits = 0;
+    if (cudaMemcpyAsync(&bits, nd.scratch, sizeof(bits), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return BM_ERR_CUDA;
+    *device_status = bits;
+    if (bits) return BM_ERR_DEVICE_TIMEOUT;
+  }
+  return BM_OK;
 }

@@ -42,7 +42,9 @@ enum bm_status_code {
   BM_ERR_DEVICE = 6,             /* current device is not compute capability 10.0 */
   BM_ERR_DEVICE_TIMEOUT = 7,     /* a bounded wait inside the kernel expired */
   BM_ERR_VARIANT = 8,            /* unknown variant id, or variant cannot run this shape */
-  BM_ERR_TILE_DIVISIBILITY = 9   /* strict mode: M/N/K not multiples of the tile */
+  BM_ERR_TILE_DIVISIBILITY = 9,  /* strict mode: M/N/K not multiples of the tile */
+  BM_ERR_SCRATCH_LIMIT = 10      /* bm_gemm_run_noalloc: call needs more scratch than its
+                                    static device array holds */
 };
 
 /* Kernel variants. BM_VARIANT_AUTO picks one from the shape. */
@@ -125,6 +127,32 @@ int bm_gemm_status(bm_gemm_handle* handle, uint32_t* device_bits);
 int bm_gemm_set_debug(bm_gemm_handle* handle, uint64_t timeout_ns, uint32_t debug_flags);
 
 void bm_gemm_destroy(bm_gemm_handle* handle);
+
+/* Size of the device scratch array used by bm_gemm_run_noalloc (bytes). */
+#define BM_NOALLOC_SCRATCH_BYTES 256
+
+/* One GEMM that allocates no device memory. No counterpart in the reference:
+ * the reference always allocates (thrust::device_vector buffers and CUTLASS
+ * launch state, host/common.cuh:125-145).
+ *
+ * For callers that cannot call cudaMalloc: programs whose device memory is
+ * owned by another allocator (for example a framework's caching allocator
+ * that has already reserved the free memory), runtimes that forbid device
+ * allocation after start-up, and latency-critical paths where cudaMalloc /
+ * cudaFree's implicit device-wide synchronisation is not acceptable.
+ *
+ * The kernel's only scratch (its 4-byte error word) lives in a file-scope
+ * static __device__ array of BM_NOALLOC_SCRATCH_BYTES bytes that every GPU
+ * loading the library keeps until the process exits. A call that would need
+ * more scratch than that is rejected with BM_ERR_SCRATCH_LIMIT.
+ * Set-up: the first call on each device (with that device current) looks up
+ * the array's device address and sets the kernel attributes; make that first
+ * call before any stream capture. Every call shares the array and clears the
+ * error word at its start on `stream`; calls that overlap on the GPU (other
+ * streams, other threads) race on it. The caller passes A, B and C as usual.
+ * device_status: NULL -> fully asynchronous; non-NULL -> the call waits for
+ * `stream` and stores the kernel's error bits there (0 = clean). */
+int bm_gemm_run_noalloc(const bm_gemm_desc* desc, void* stream, uint32_t* device_status);
 
 /* Device-side input generator, bit-identical to the CPU oracle's
  * (oracle/bm_oracle.c, bmo_input_value):
