@@ -40,9 +40,11 @@ VARIANT_2CTA_256x256 = 1
 VARIANT_1CTA_128x256 = 2
 VARIANT_1CTA_128x128 = 3
 VARIANT_2CTA_256x128 = 4
-VARIANTS = (1, 2, 3, 4)
+VARIANT_2CTA_256x512 = 5
+VARIANTS = (1, 2, 3, 4, 5)
 # (tile_m, tile_n, stages) per variant
-VARIANT_TILES = {1: (256, 256, 6), 2: (128, 256, 4), 3: (128, 128, 6), 4: (256, 128, 6)}
+VARIANT_TILES = {1: (256, 256, 6), 2: (128, 256, 4), 3: (128, 128, 6), 4: (256, 128, 6),
+                 5: (256, 512, 4)}
 
 DEBUG_EPILOGUE_WAITS_NEVER = 1
 

@@ -33,16 +33,26 @@ struct VariantInfo {
   int id;
   const char* name;
   int cta_group;
-  int tile_n;
+  int mma_n;   // N of one MMA instruction
+  int num_n;   // MMAs per K step sharing one A tile
   int stages;
 };
 
+// X(id, cta_group, mma_n, num_n, stages): every compiled kernel variant.
+#define BM_FOR_EACH_VARIANT(X)                 \
+  X(BM_VARIANT_2CTA_256x256, 2, 256, 1, 6)     \
+  X(BM_VARIANT_1CTA_128x256, 1, 256, 1, 4)     \
+  X(BM_VARIANT_1CTA_128x128, 1, 128, 1, 6)     \
+  X(BM_VARIANT_2CTA_256x128, 2, 128, 1, 6)     \
+  X(BM_VARIANT_2CTA_256x512, 2, 256, 2, 4)
+
 const VariantInfo kVariants[] = {
-    {BM_VARIANT_AUTO, "auto", 0, 0, 0},
-    {BM_VARIANT_2CTA_256x256, "sm100_tcgen05_2cta_256x256x64_s6", 2, 256, 6},
-    {BM_VARIANT_1CTA_128x256, "sm100_tcgen05_1cta_128x256x64_s4", 1, 256, 4},
-    {BM_VARIANT_1CTA_128x128, "sm100_tcgen05_1cta_128x128x64_s6", 1, 128, 6},
-    {BM_VARIANT_2CTA_256x128, "sm100_tcgen05_2cta_256x128x64_s6", 2, 128, 6},
+    {BM_VARIANT_AUTO, "auto", 0, 0, 0, 0},
+    {BM_VARIANT_2CTA_256x256, "sm100_tcgen05_2cta_256x256x64_s6", 2, 256, 1, 6},
+    {BM_VARIANT_1CTA_128x256, "sm100_tcgen05_1cta_128x256x64_s4", 1, 256, 1, 4},
+    {BM_VARIANT_1CTA_128x128, "sm100_tcgen05_1cta_128x128x64_s6", 1, 128, 1, 6},
+    {BM_VARIANT_2CTA_256x128, "sm100_tcgen05_2cta_256x128x64_s6", 2, 128, 1, 6},
+    {BM_VARIANT_2CTA_256x512, "sm100_tcgen05_2cta_256x512x64_s4", 2, 256, 2, 4},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 
@@ -68,9 +78,9 @@ struct bm_gemm_handle {
 
 namespace {
 
-template <int kCtaGroup, int kBN, int kStages, bool kMn>
+template <int kCtaGroup, int kBN, int kNumN, int kStages, bool kMn>
 cudaError_t launch_variant(const bm_gemm_handle* h, cudaStream_t stream) {
-  using Cfg = GemmConfig<kCtaGroup, kBN, kStages, kMn>;
+  using Cfg = GemmConfig<kCtaGroup, kBN, kNumN, kStages, kMn>;
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(static_cast<unsigned>(h->grid), 1, 1);
@@ -84,7 +94,7 @@ cudaError_t launch_variant(const bm_gemm_handle* h, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, bm::bm_gemm_sm100_kernel<kCtaGroup, kBN, kStages, kMn>,
+  return cudaLaunchKernelEx(&cfg, bm::bm_gemm_sm100_kernel<kCtaGroup, kBN, kNumN, kStages, kMn>,
                             h->tmap_a, h->tmap_b, h->tmap_c, h->params);
 }
 
@@ -97,9 +107,9 @@ struct GeometryCache {
 std::mutex g_cache_mutex;
 GeometryCache g_cache[64][kNumVariants][2];
 
-template <int kCtaGroup, int kBN, int kStages, bool kMn>
+template <int kCtaGroup, int kBN, int kNumN, int kStages, bool kMn>
 cudaError_t geometry(int device, int sm_count, int variant, int* max_clusters, int* smem) {
-  using Cfg = GemmConfig<kCtaGroup, kBN, kStages, kMn>;
+  using Cfg = GemmConfig<kCtaGroup, kBN, kNumN, kStages, kMn>;
   static_assert(Cfg::kSmemBytes > 116 * 1024,
                 "one CTA per SM is required: each CTA allocates all the TMEM it uses");
   *smem = Cfg::kSmemBytes;
@@ -109,7 +119,7 @@ cudaError_t geometry(int device, int sm_count, int variant, int* max_clusters, i
     *max_clusters = gc.max_clusters;
     return cudaSuccess;
   }
-  auto kernel = bm::bm_gemm_sm100_kernel<kCtaGroup, kBN, kStages, kMn>;
+  auto kernel = bm::bm_gemm_sm100_kernel<kCtaGroup, kBN, kNumN, kStages, kMn>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
@@ -242,7 +252,7 @@ int bm_gemm_check(const bm_gemm_desc* d) {
   const int v = pick_variant(d);
   if (v <= 0 || v >= kNumVariants) return BM_ERR_VARIANT;
   if (d->strict_tiles) {
-    const int tm = 128 * kVariants[v].cta_group, tn = kVariants[v].tile_n;
+    const int tm = 128 * kVariants[v].cta_group, tn = kVariants[v].mma_n * kVariants[v].num_n;
     if (d->m % tm || d->n % tn || d->k % 64) return BM_ERR_TILE_DIVISIBILITY;
   }
   return BM_OK;
@@ -273,10 +283,10 @@ int bm_gemm_prepare(const bm_gemm_desc* d, bm_gemm_handle** out) {
   h->device = device;
   h->cta_group = kVariants[v].cta_group;
   h->tile_m = 128 * h->cta_group;
-  h->tile_n = kVariants[v].tile_n;
+  h->tile_n = kVariants[v].mma_n * kVariants[v].num_n;
   h->stages = kVariants[v].stages;
 
-  const int rows_b = h->tile_n / h->cta_group;
+  const int rows_b = kVariants[v].mma_n / h->cta_group;  // B rows per CTA per MMA
   bool ok;
   if (r.nt) {
     ok = encode_2d(&h->tmap_a, d->a, d->m, d->k, r.lda, 64, 64, true) &&
@@ -294,19 +304,16 @@ int bm_gemm_prepare(const bm_gemm_desc* d, bm_gemm_handle** out) {
   int max_clusters = 0, smem = 0;
   cudaError_t e = cudaErrorInvalidValue;
   switch (v * 2 + (r.nt ? 1 : 0)) {
-#define BM_CASE(VID, CG, BN, ST)                                                        \
+#define BM_CASE(VID, CG, BN, NN, ST)                                                    \
   case VID * 2 + 0:                                                                     \
-    e = geometry<CG, BN, ST, false>(device, sms, VID, &max_clusters, &smem);            \
-    h->launch = &launch_variant<CG, BN, ST, false>;                                     \
+    e = geometry<CG, BN, NN, ST, false>(device, sms, VID, &max_clusters, &smem);        \
+    h->launch = &launch_variant<CG, BN, NN, ST, false>;                                 \
     break;                                                                              \
   case VID * 2 + 1:                                                                     \
-    e = geometry<CG, BN, ST, true>(device, sms, VID, &max_clusters, &smem);             \
-    h->launch = &launch_variant<CG, BN, ST, true>;                                      \
+    e = geometry<CG, BN, NN, ST, true>(device, sms, VID, &max_clusters, &smem);         \
+    h->launch = &launch_variant<CG, BN, NN, ST, true>;                                  \
     break;
-    BM_CASE(BM_VARIANT_2CTA_256x256, 2, 256, 6)
-    BM_CASE(BM_VARIANT_1CTA_128x256, 1, 256, 4)
-    BM_CASE(BM_VARIANT_1CTA_128x128, 1, 128, 6)
-    BM_CASE(BM_VARIANT_2CTA_256x128, 2, 128, 6)
+    BM_FOR_EACH_VARIANT(BM_CASE)
 #undef BM_CASE
     default: break;
   }
@@ -327,6 +334,7 @@ int bm_gemm_prepare(const bm_gemm_desc* d, bm_gemm_handle** out) {
   p.group_m = 8;
   p.timeout_ns = kDefaultTimeoutNs;
   p.debug = 0;
+  p.stats = nullptr;
   const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
   h->grid = clusters * h->cta_group;
 
@@ -356,7 +364,7 @@ int bm_gemm_query(const bm_gemm_handle* h, bm_launch_info* info) {
   info->smem_bytes = h->smem_bytes;
   info->grid[0] = h->grid;
   info->grid[1] = info->grid[2] = 1;
-  info->block[0] = 192;
+  info->block[0] = bm::kGemmThreads;
   info->block[1] = info->block[2] = 1;
   info->cluster[0] = h->cta_group;
   info->cluster[1] = info->cluster[2] = 1;
@@ -387,6 +395,16 @@ int bm_gemm_set_debug(bm_gemm_handle* h, uint64_t timeout_ns, uint32_t flags) {
   h->params.debug = flags;
   return BM_OK;
 }
+
+#if defined(BM_KERNEL_STATS)
+// Diagnostics builds only (not declared in the public header): attach a
+// device buffer of grid x 16 uint64 counters to a handle.
+int bm_gemm_debug_attach_stats(bm_gemm_handle* h, void* stats) {
+  if (!h) return BM_ERR_INVALID_ARGUMENT;
+  h->params.stats = static_cast<unsigned long long*>(stats);
+  return BM_OK;
+}
+#endif
 
 void bm_gemm_destroy(bm_gemm_handle* h) {
   if (!h) return;
@@ -504,9 +522,9 @@ extern "C" int bm_gemm_run_noalloc(const bm_gemm_desc* d, void* stream, uint32_t
   h.device = device;
   h.cta_group = kVariants[v].cta_group;
   h.tile_m = 128 * h.cta_group;
-  h.tile_n = kVariants[v].tile_n;
+  h.tile_n = kVariants[v].mma_n * kVariants[v].num_n;
   h.stages = kVariants[v].stages;
-  const int rows_b = h.tile_n / h.cta_group;
+  const int rows_b = kVariants[v].mma_n / h.cta_group;  // B rows per CTA per MMA
   bool ok;
   if (r.nt) {
     ok = encode_2d(&h.tmap_a, d->a, d->m, d->k, r.lda, 64, 64, true) &&
@@ -521,19 +539,16 @@ extern "C" int bm_gemm_run_noalloc(const bm_gemm_desc* d, void* stream, uint32_t
   int max_clusters = 0, smem = 0;
   cudaError_t e = cudaErrorInvalidValue;
   switch (v * 2 + (r.nt ? 1 : 0)) {
-#define BM_NOALLOC_CASE(VID, CG, BN, ST)                                               \
+#define BM_NOALLOC_CASE(VID, CG, BN, NN, ST)                                           \
   case VID * 2 + 0:                                                                    \
-    e = geometry<CG, BN, ST, false>(device, sms, VID, &max_clusters, &smem);           \
-    h.launch = &launch_variant<CG, BN, ST, false>;                                     \
+    e = geometry<CG, BN, NN, ST, false>(device, sms, VID, &max_clusters, &smem);       \
+    h.launch = &launch_variant<CG, BN, NN, ST, false>;                                 \
     break;                                                                             \
   case VID * 2 + 1:                                                                    \
-    e = geometry<CG, BN, ST, true>(device, sms, VID, &max_clusters, &smem);            \
-    h.launch = &launch_variant<CG, BN, ST, true>;                                      \
+    e = geometry<CG, BN, NN, ST, true>(device, sms, VID, &max_clusters, &smem);        \
+    h.launch = &launch_variant<CG, BN, NN, ST, true>;                                  \
     break;
-    BM_NOALLOC_CASE(BM_VARIANT_2CTA_256x256, 2, 256, 6)
-    BM_NOALLOC_CASE(BM_VARIANT_1CTA_128x256, 1, 256, 4)
-    BM_NOALLOC_CASE(BM_VARIANT_1CTA_128x128, 1, 128, 6)
-    BM_NOALLOC_CASE(BM_VARIANT_2CTA_256x128, 2, 128, 6)
+    BM_FOR_EACH_VARIANT(BM_NOALLOC_CASE)
 #undef BM_NOALLOC_CASE
     default: break;
   }
@@ -551,6 +566,7 @@ extern "C" int bm_gemm_run_noalloc(const bm_gemm_desc* d, void* stream, uint32_t
   p.group_m = 8;
   p.timeout_ns = kDefaultTimeoutNs;
   p.debug = 0;
+  p.stats = nullptr;
   p.status = nd.scratch;
   const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
   h.grid = clusters * h.cta_group;

@@ -13,14 +13,20 @@
 //
 //   warp 0      TMA producer: fills a kStages-deep shared-memory ring
 //   warp 1      MMA issuer: one thread issues tcgen05.mma into TMEM; owns TMEM
-//   warps 2..5  epilogue: TMEM -> registers -> FP16 -> smem -> TMA store,
-//               overlapped with the next tile's mainloop via two TMEM
-//               accumulator buffers
+//   warps 2..9  epilogue: TMEM -> registers -> FP16 -> smem -> TMA store;
+//               two warps per TMEM lane quarter, each draining half the columns
 //
-// kCtaGroup == 2 runs each tile on a CTA pair (cluster 2x1) with
-// tcgen05.mma.cta_group::2: the pair computes a 256 x kBN tile, each CTA loads
-// its own 128 rows of A and kBN/2 rows of B (no multicast), and each CTA's
-// TMEM holds its 128 output rows.
+// Tile geometry (template parameters):
+//   kCtaGroup  1: one CTA computes 128 rows; 2: a CTA pair (cluster 2x1) runs
+//              tcgen05.mma.cta_group::2 and computes 256 rows, each CTA holding
+//              its own 128 rows of A and half of every B block (no multicast).
+//   kBN        N of one MMA instruction (128 or 256).
+//   kNumN      MMAs per K step that share the same A tile (1 or 2): the tile
+//              is kBN * kNumN wide, so every A byte brought on chip feeds
+//              kNumN MMAs. kNumN = 2 with kBN = 256 fills all 512 TMEM columns.
+// With room for two accumulators in TMEM (kAccStages = 2) the epilogue of tile
+// i overlaps the mainloop of tile i+1; with one, the producer still prefetches
+// the next tile's first stages while the epilogue drains TMEM.
 //
 // Every wait is bounded (ptx::bm_wait); on expiry the CTA records an error
 // code in the device status word, tells its other roles to stop, drains its
@@ -48,31 +54,66 @@ enum : uint32_t {
 
 struct GemmParams {
   int m, n, k;
-  int tiles_m, tiles_n;  // tile grid in units of (kTileM x kBN)
+  int tiles_m, tiles_n;  // tile grid in units of (kTileM x kTileN)
   int num_tiles;
   int k_blocks;          // ceil(k / 64)
   int group_m;           // rasterization: tiles of group_m M-blocks share B in L2
   uint32_t* status;      // device error word (OR of kStatus* bits)
   uint64_t timeout_ns;   // bound on every mbarrier wait
   uint32_t debug;        // kDebug* flags; 0 in production
+  unsigned long long* stats;  // per-CTA cycle counters; only read in BM_KERNEL_STATS builds
 };
 
-template <int kCtaGroup, int kBN, int kStages, bool kMnMajor>
+// Opt-in pipeline counters (build with -DBM_KERNEL_STATS): per CTA, cycles
+// spent in each role's waits and a few timestamps, for diagnosing where the
+// mainloop stalls. Product builds compile them out entirely.
+enum StatSlot : int {
+  kStatTotal = 0, kStatProdWait, kStatProdWaits, kStatMmaFullWait, kStatMmaFullWaits,
+  kStatMmaTmemWait, kStatMmaTmemWaits, kStatEpiWait, kStatEpiWaits, kStatEpiBusy,
+  kStatTiles, kStatKBlocks, kStatT0, kStatT1, kStatMmaFirst, kStatMmaLast, kNumStats = 16
+};
+
+#if defined(BM_KERNEL_STATS)
+__device__ __forceinline__ bool stat_wait(uint32_t bar, uint32_t parity, uint64_t timeout_ns,
+                                          const volatile uint32_t* abort_flag,
+                                          unsigned long long& cycles, unsigned long long& count) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  const bool ok = ptx::bm_wait(bar, parity, timeout_ns, abort_flag);
+  cycles += static_cast<unsigned long long>(clock64() - t0);
+  count += 1;
+  return ok;
+}
+#define BM_WAIT(bar, par, to, ab, CYC, CNT) stat_wait(bar, par, to, ab, st[CYC], st[CNT])
+#else
+#define BM_WAIT(bar, par, to, ab, CYC, CNT) ptx::bm_wait(bar, par, to, ab)
+#endif
+
+constexpr int kEpiWarps = 8;                        // two per TMEM lane quarter
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;   // producer + MMA + epilogue warps
+
+template <int kCtaGroup, int kBN, int kNumN, int kStages, bool kMnMajor>
 struct GemmConfig {
-  static constexpr int kThreads = 192;
-  static constexpr int kBK = 64;                       // one 128-byte swizzle row of FP16
-  static constexpr int kRowsA = 128;                   // A rows per CTA (TMEM lanes)
-  static constexpr int kTileM = 128 * kCtaGroup;       // output rows per tile
-  static constexpr int kRowsB = kBN / kCtaGroup;       // B rows loaded per CTA
+  static constexpr int kThreads = kGemmThreads;
+  static constexpr int kBK = 64;                        // one 128-byte swizzle row of FP16
+  static constexpr int kRowsA = 128;                    // A rows per CTA (TMEM lanes)
+  static constexpr int kTileM = 128 * kCtaGroup;        // output rows per tile
+  static constexpr int kTileN = kBN * kNumN;            // output columns per tile
   static constexpr int kMmaM = 128 * kCtaGroup;
-  static constexpr int kBytesA = kRowsA * kBK * 2;     // 16 KB
-  static constexpr int kBytesB = kRowsB * kBK * 2;
+  static constexpr int kRowsBPerMma = kBN / kCtaGroup;  // B rows per CTA for one MMA
+  static constexpr int kBytesA = kRowsA * kBK * 2;      // 16 KB
+  static constexpr int kBytesBPerMma = kRowsBPerMma * kBK * 2;
+  static constexpr int kBytesB = kBytesBPerMma * kNumN;
   static constexpr int kStageBytes = kBytesA + kBytesB;
-  static constexpr int kEpiBoxRows = 32;               // one warp's TMEM lane quarter
+  static constexpr int kAccCols = kBN * kNumN;          // TMEM columns of one accumulator
+  static constexpr int kAccStages = (2 * kAccCols <= 512) ? 2 : 1;
+  static constexpr int kTmemCols = kAccCols * kAccStages;
+  static constexpr int kChunks = kAccCols / 32;         // epilogue chunks of 32 columns
+  static constexpr int kChunksPerWarp = kChunks / 2;    // each lane quarter has two warps
+  static constexpr int kEpiBoxRows = 32;                // one warp's TMEM lane quarter
   static constexpr int kEpiBoxCols = 32;
   static constexpr int kEpiBufBytes = kEpiBoxRows * kEpiBoxCols * 2;  // 2 KB
-  static constexpr int kEpiBytes = 4 * 2 * kEpiBufBytes;              // 4 warps x 2 buffers
-  static constexpr int kTmemCols = 2 * kBN;            // two accumulator buffers
+  static constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;      // 2 buffers per warp
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kBytesA;
   static constexpr int kOffEpi = kOffB + kStages * kBytesB;
@@ -84,11 +125,13 @@ struct GemmConfig {
   static constexpr int kSmemBytes = kOffAbort + 4 + 1024;  // + alignment slack
   static constexpr uint32_t kIdesc = make_idesc_f16_f32(kMmaM, kBN, kMnMajor);
 
-  static_assert(kBN % 64 == 0 && kBN <= 256, "kBN must be a multiple of 64, at most 256");
-  static_assert(kRowsB % 64 == 0, "B rows per CTA must be a multiple of 64");
-  static_assert(kTmemCols <= 512, "two accumulators must fit in TMEM");
+  static_assert(kBN == 128 || kBN == 256, "kBN must be 128 or 256");
+  static_assert(kNumN == 1 || kNumN == 2, "kNumN must be 1 or 2");
+  static_assert(kRowsBPerMma % 64 == 0, "B rows per CTA and MMA must be a multiple of 64");
+  static_assert(kTmemCols <= 512, "accumulators must fit in TMEM");
   static_assert((kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation must be a power of 2");
-  static_assert(kBytesA % 1024 == 0 && kBytesB % 1024 == 0, "stages keep 1 KB alignment");
+  static_assert(kChunksPerWarp % 2 == 0, "each epilogue warp processes chunks in pairs");
+  static_assert(kBytesA % 1024 == 0 && kBytesBPerMma % 1024 == 0, "stages keep 1 KB alignment");
   static_assert(kSmemBytes <= 232448, "shared memory budget (227 KB) exceeded");
 };
 
@@ -104,14 +147,17 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& 
   nb = in_group / rows;
 }
 
-template <int kCtaGroup, int kBN, int kStages, bool kMnMajor>
-__global__ void __launch_bounds__(192, 1)
+template <int kCtaGroup, int kBN, int kNumN, int kStages, bool kMnMajor>
+__global__ void __launch_bounds__(kGemmThreads, 1)
 bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ CUtensorMap tmap_c, const GemmParams p) {
-  using Cfg = GemmConfig<kCtaGroup, kBN, kStages, kMnMajor>;
+  using Cfg = GemmConfig<kCtaGroup, kBN, kNumN, kStages, kMnMajor>;
   extern __shared__ uint8_t smem_raw[];
 
+#if defined(BM_KERNEL_STATS)
+  const unsigned long long g_entry = ptx::globaltimer_ns();
+#endif
   // 1 KB alignment for the 128-byte-swizzled tiles. Both CTAs of a pair run
   // the same code, so the offsets (and hence the MMA descriptors) agree.
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
@@ -149,7 +195,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(tfull_bar(a), 1);                // one tcgen05.commit per tile
-      ptx::mbar_init(tempty_bar(a), 4 * kCtaGroup);   // one arrive per epilogue warp
+      ptx::mbar_init(tempty_bar(a), kEpiWarps * kCtaGroup);  // one arrive per epilogue warp
     }
     ptx::mbar_init(drain_bar, 1);
     ptx::mbar_init(never_bar, 1);
@@ -165,6 +211,10 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
   if constexpr (kCtaGroup == 2) ptx::cluster_sync();  // peer barriers initialised
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+#if defined(BM_KERNEL_STATS)
+  unsigned long long st[kNumStats] = {};
+  const long long t_begin = clock64();
+#endif
 
   auto fail = [&](uint32_t bit) {
     *abort_flag = 1u;
@@ -181,9 +231,10 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         int mb, nb;
         tile_coords(tile, p, mb, nb);
         const int m0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * Cfg::kRowsA;
-        const int n0 = nb * kBN + static_cast<int>(cta_rank) * Cfg::kRowsB;
+        // this CTA's B rows for MMA j: nb*kTileN + j*kBN + rank*kRowsBPerMma + [0, kRowsBPerMma)
+        const int n0 = nb * Cfg::kTileN + static_cast<int>(cta_rank) * Cfg::kRowsBPerMma;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!ptx::bm_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag)) {
+          if (!BM_WAIT(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, kStatProdWait, kStatProdWaits)) {
             fail(kStatusProducerTimeout);
             ok = false;
             break;
@@ -191,32 +242,33 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           const int k0 = kb * Cfg::kBK;
           const uint32_t a_dst = sA + stage * Cfg::kBytesA;
           const uint32_t b_dst = sB + stage * Cfg::kBytesB;
+          // Completion bytes go to this CTA's barrier (1 CTA) or the pair
+          // leader's barrier (2 CTAs), which expects both CTAs' bytes.
+          uint32_t fb;
           if constexpr (kCtaGroup == 1) {
-            const uint32_t fb = full_bar(stage);
+            fb = full_bar(stage);
             ptx::mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-            if constexpr (kMnMajor) {
-              ptx::tma_load_2d(a_dst, &tmap_a, fb, m0, k0);
-              ptx::tma_load_2d(a_dst + 8192, &tmap_a, fb, m0 + 64, k0);
-#pragma unroll
-              for (int j = 0; j < Cfg::kRowsB / 64; ++j)
-                ptx::tma_load_2d(b_dst + 8192 * j, &tmap_b, fb, n0 + 64 * j, k0);
-            } else {
-              ptx::tma_load_2d(a_dst, &tmap_a, fb, k0, m0);
-              ptx::tma_load_2d(b_dst, &tmap_b, fb, k0, n0);
-            }
           } else {
-            const uint32_t fb_leader = ptx::mapa(full_bar(stage), 0);
+            fb = ptx::mapa(full_bar(stage), 0);
             if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * Cfg::kStageBytes);
-            if constexpr (kMnMajor) {
-              ptx::tma_load_2d_pair(a_dst, &tmap_a, fb_leader, m0, k0);
-              ptx::tma_load_2d_pair(a_dst + 8192, &tmap_a, fb_leader, m0 + 64, k0);
+          }
+          auto load = [&](uint32_t dst, const CUtensorMap* map, int x, int y) {
+            if constexpr (kCtaGroup == 1) ptx::tma_load_2d(dst, map, fb, x, y);
+            else ptx::tma_load_2d_pair(dst, map, fb, x, y);
+          };
+          if constexpr (kMnMajor) {
+            load(a_dst, &tmap_a, m0, k0);
+            load(a_dst + 8192, &tmap_a, m0 + 64, k0);
 #pragma unroll
-              for (int j = 0; j < Cfg::kRowsB / 64; ++j)
-                ptx::tma_load_2d_pair(b_dst + 8192 * j, &tmap_b, fb_leader, n0 + 64 * j, k0);
-            } else {
-              ptx::tma_load_2d_pair(a_dst, &tmap_a, fb_leader, k0, m0);
-              ptx::tma_load_2d_pair(b_dst, &tmap_b, fb_leader, k0, n0);
-            }
+            for (int j = 0; j < kNumN; ++j)
+#pragma unroll
+              for (int q = 0; q < Cfg::kRowsBPerMma / 64; ++q)
+                load(b_dst + j * Cfg::kBytesBPerMma + 8192 * q, &tmap_b, n0 + j * kBN + 64 * q, k0);
+          } else {
+            load(a_dst, &tmap_a, k0, m0);
+#pragma unroll
+            for (int j = 0; j < kNumN; ++j)
+              load(b_dst + j * Cfg::kBytesBPerMma, &tmap_b, k0, n0 + j * kBN);
           }
           if (++stage == kStages) {
             stage = 0;
@@ -249,14 +301,14 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       bool ok = true;
       const uint32_t peer = 1u;
       for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters) {
-        if (!ptx::bm_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, abort_flag)) {
+        if (!BM_WAIT(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, abort_flag, kStatMmaTmemWait, kStatMmaTmemWaits)) {
           fail(kStatusMmaTimeout);
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!ptx::bm_wait(full_bar(stage), phase, p.timeout_ns, abort_flag)) {
+          if (!BM_WAIT(full_bar(stage), phase, p.timeout_ns, abort_flag, kStatMmaFullWait, kStatMmaFullWaits)) {
             fail(kStatusMmaTimeout);
             ok = false;
             break;
@@ -266,25 +318,31 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           const uint32_t b_base = sB + stage * Cfg::kBytesB;
 #pragma unroll
           for (int ks = 0; ks < Cfg::kBK / 16; ++ks) {
-            uint64_t a_desc, b_desc;
-            if constexpr (kMnMajor) {
-              // 64 MN-elements per 128-byte row, one row per k; 8-row swizzle
-              // atoms are 1 KB apart (SBO); 64-element MN chunks 8 KB apart
-              // (LBO). One K=16 step covers 16 rows = 2 KB.
-              a_desc = ptx::smem_desc_sw128(a_base + ks * 2048, 8192, 1024);
-              b_desc = ptx::smem_desc_sw128(b_base + ks * 2048, 8192, 1024);
-            } else {
-              // One 128-byte row (64 k) per M/N row; 8-row atoms 1 KB apart.
-              // One K=16 step advances 32 bytes inside the swizzled row.
-              a_desc = ptx::smem_desc_sw128(a_base + ks * 32, 16, 1024);
-              b_desc = ptx::smem_desc_sw128(b_base + ks * 32, 16, 1024);
+            // MN-major: 64 MN-elements per 128-byte row, one row per k; 8-row
+            // swizzle atoms 1 KB apart (SBO); 64-element MN chunks 8 KB apart
+            // (LBO); one K=16 step is 16 rows = 2 KB.
+            // K-major: one 128-byte row (64 k) per M/N row; 8-row atoms 1 KB
+            // apart; one K=16 step advances 32 bytes inside the swizzled row.
+            const uint32_t koff = kMnMajor ? ks * 2048u : ks * 32u;
+            const uint32_t lbo = kMnMajor ? 8192u : 16u;
+            const uint64_t a_desc = ptx::smem_desc_sw128(a_base + koff, lbo, 1024);
+#pragma unroll
+            for (int j = 0; j < kNumN; ++j) {
+              const uint64_t b_desc =
+                  ptx::smem_desc_sw128(b_base + j * Cfg::kBytesBPerMma + koff, lbo, 1024);
+#if defined(BM_KERNEL_STATS)
+              if (st[kStatMmaFirst] == 0) st[kStatMmaFirst] = ptx::globaltimer_ns();
+#endif
+              ptx::mma_f16<kCtaGroup>(d_tmem + static_cast<uint32_t>(j * kBN), a_desc, b_desc,
+                                      Cfg::kIdesc, (kb > 0 || ks > 0) ? 1u : 0u);
             }
-            ptx::mma_f16<kCtaGroup>(d_tmem, a_desc, b_desc, Cfg::kIdesc,
-                                    (kb > 0 || ks > 0) ? 1u : 0u);
           }
           // Free this stage in every CTA that loaded into it.
           ptx::mma_commit<kCtaGroup>(empty_bar(stage));
           if constexpr (kCtaGroup == 2) ptx::mma_commit<kCtaGroup>(ptx::mapa(empty_bar(stage), peer));
+#if defined(BM_KERNEL_STATS)
+          st[kStatKBlocks] += 1;
+#endif
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -294,7 +352,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         // Accumulator complete -> both CTAs' epilogues.
         ptx::mma_commit<kCtaGroup>(tfull_bar(acc));
         if constexpr (kCtaGroup == 2) ptx::mma_commit<kCtaGroup>(ptx::mapa(tfull_bar(acc), peer));
-        if (++acc == 2) {
+        if (++acc == Cfg::kAccStages) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -306,15 +364,20 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (!ptx::bm_wait(drain_bar, 0u, p.timeout_ns, &no_abort)) {
         atomicOr(p.status, kStatusDrainTimeout);
       }
+#if defined(BM_KERNEL_STATS)
+      st[kStatMmaLast] = ptx::globaltimer_ns();
+#endif
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
-    const int ew = warp - 2;       // epilogue warp index 0..3 (staging buffers)
+    const int ew = warp - 2;       // epilogue warp index 0..7 (staging buffers)
+    const int chunk0 = (ew / 4) * Cfg::kChunksPerWarp;  // this warp's half of the columns
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tempty_leader0 = (kCtaGroup == 2) ? ptx::mapa(tempty_bar(0), 0) : tempty_bar(0);
     const uint32_t tempty_leader1 = (kCtaGroup == 2) ? ptx::mapa(tempty_bar(1), 0) : tempty_bar(1);
+    const bool odd = (lane & 1) != 0;
     bool ok = true;
     if (p.debug & kDebugEpilogueWaitsNever) {
       // Fault-injection hook for tests: nothing ever arrives on never_bar,
@@ -327,26 +390,66 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
     int acc = 0;
     uint32_t acc_phase = 0;
-    int chunk = 0;  // running chunk count -> staging buffer parity
+    int chunk_count = 0;  // running chunk count -> staging buffer parity
+
+    // Convert one 32x32 chunk (this warp's 32 rows x 32 columns) to FP16 and
+    // store it with one TMA box. Lane pairs swap halves so that each lane
+    // writes one 32-bit word holding two consecutive rows of one column:
+    // column-major C, conflict-free shared-memory stores.
+    auto store_chunk = [&](const uint32_t (&r)[32], int row0, int col) {
+      const uint32_t buf =
+          sEpi + static_cast<uint32_t>((ew * 2 + (chunk_count & 1)) * Cfg::kEpiBufBytes);
+      ++chunk_count;
+      if (lane == 0) ptx::bulk_wait_group_read<1>();  // buffer from 2 chunks ago is free
+      __syncwarp();
+      uint32_t* wb = reinterpret_cast<uint32_t*>(smem + (buf - base));
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t send = odd ? r[2 * i] : r[2 * i + 1];
+        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+        const float lo = __uint_as_float(odd ? recv : r[2 * i]);       // even row
+        const float hi = __uint_as_float(odd ? r[2 * i + 1] : recv);   // odd row
+        const __half2 h = __floats2half2_rn(lo, hi);
+        wb[(2 * i + (odd ? 1 : 0)) * 16 + (lane >> 1)] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        ptx::tma_store_2d(&tmap_c, buf, row0, col);
+        ptx::bulk_commit_group();
+      }
+    };
+
     for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
-      if (!ptx::bm_wait(tfull_bar(acc), acc_phase, p.timeout_ns, abort_flag)) {
+      if (!BM_WAIT(tfull_bar(acc), acc_phase, p.timeout_ns, abort_flag, kStatEpiWait, kStatEpiWaits)) {
         if (lane == 0) fail(kStatusEpilogueTimeout);
         break;
       }
       ptx::tc_fence_after();
+#if defined(BM_KERNEL_STATS)
+      const long long t_epi = clock64();
+#endif
       const int row0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * 128 + quarter * 32;
-      const int col0 = nb * kBN;
-      const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * kBN);
+      const int col0 = nb * Cfg::kTileN;
+      const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
+      // Two register buffers: the TMEM load of chunk c+1 is in flight while
+      // chunk c is converted and stored.
+      uint32_t ra[32], rb[32];
+      const int c_end = chunk0 + Cfg::kChunksPerWarp;
+      ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(chunk0 * 32), ra);
+      ptx::tmem_wait_ld();
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c, ++chunk) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(c * 32), r);
+      for (int c = chunk0; c < c_end; c += 2) {
+        ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>((c + 1) * 32), rb);
+        store_chunk(ra, row0, col0 + c * 32);
         ptx::tmem_wait_ld();
-        if (c == kBN / 32 - 1) {
-          // All of this warp's TMEM reads for the tile are done: hand the
-          // accumulator back to the MMA issuer before the stores.
+        if (c + 2 < c_end) {
+          ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>((c + 2) * 32), ra);
+        } else {
+          // Every TMEM read of this tile has completed: hand the
+          // accumulator back to the MMA issuer before the last stores.
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) {
@@ -355,22 +458,14 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
             else ptx::mbar_arrive(tb);
           }
         }
-        const uint32_t buf = sEpi + static_cast<uint32_t>((ew * 2 + (chunk & 1)) * Cfg::kEpiBufBytes);
-        if (lane == 0) ptx::bulk_wait_group_read<1>();  // buffer from 2 chunks ago is free
-        __syncwarp();
-        __half* hb = reinterpret_cast<__half*>(smem + (buf - base));
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          hb[j * 32 + lane] = __float2half_rn(__uint_as_float(r[j]));
-        }
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          ptx::tma_store_2d(&tmap_c, buf, row0, col0 + c * 32);
-          ptx::bulk_commit_group();
-        }
+        store_chunk(rb, row0, col0 + (c + 1) * 32);
+        ptx::tmem_wait_ld();
       }
-      if (++acc == 2) {
+#if defined(BM_KERNEL_STATS)
+      st[kStatEpiBusy] += static_cast<unsigned long long>(clock64() - t_epi);
+      st[kStatTiles] += 1;
+#endif
+      if (++acc == Cfg::kAccStages) {
         acc = 0;
         acc_phase ^= 1u;
       }
@@ -378,6 +473,34 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     if (lane == 0) ptx::bulk_wait_group<0>();
     __syncwarp();
   }
+
+#if defined(BM_KERNEL_STATS)
+  if (p.stats != nullptr && lane == 0) {
+    st[kStatTotal] = static_cast<unsigned long long>(clock64() - t_begin);
+    unsigned long long* out = p.stats + static_cast<size_t>(blockIdx.x) * kNumStats;
+    // one writer per role: producer (warp 0), MMA (warp 1), first epilogue warp (warp 2)
+    if (warp == 0) {
+      out[kStatTotal] = st[kStatTotal];
+      out[kStatProdWait] = st[kStatProdWait];
+      out[kStatProdWaits] = st[kStatProdWaits];
+    } else if (warp == 1) {
+      out[kStatMmaFirst] = st[kStatMmaFirst];
+      out[kStatMmaLast] = st[kStatMmaLast];
+      out[kStatMmaFullWait] = st[kStatMmaFullWait];
+      out[kStatMmaFullWaits] = st[kStatMmaFullWaits];
+      out[kStatMmaTmemWait] = st[kStatMmaTmemWait];
+      out[kStatMmaTmemWaits] = st[kStatMmaTmemWaits];
+      out[kStatKBlocks] = st[kStatKBlocks];
+    } else if (warp == 2) {
+      out[kStatT0] = g_entry;
+      out[kStatT1] = ptx::globaltimer_ns();
+      out[kStatEpiWait] = st[kStatEpiWait];
+      out[kStatEpiWaits] = st[kStatEpiWaits];
+      out[kStatEpiBusy] = st[kStatEpiBusy];
+      out[kStatTiles] = st[kStatTiles];
+    }
+  }
+#endif
 
   // ------------------------------------------------------------ teardown
   ptx::tc_fence_before();

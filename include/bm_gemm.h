@@ -53,7 +53,9 @@ enum bm_variant {
   BM_VARIANT_2CTA_256x256 = 1, /* cta_group::2 pair, 256x256 tile, 6 stages */
   BM_VARIANT_1CTA_128x256 = 2, /* cta_group::1, 128x256 tile, 4 stages */
   BM_VARIANT_1CTA_128x128 = 3, /* cta_group::1, 128x128 tile, 6 stages */
-  BM_VARIANT_2CTA_256x128 = 4  /* cta_group::2 pair, 256x128 tile, 6 stages */
+  BM_VARIANT_2CTA_256x128 = 4, /* cta_group::2 pair, 256x128 tile, 6 stages */
+  BM_VARIANT_2CTA_256x512 = 5  /* cta_group::2 pair, 256x512 tile (two N=256 MMAs share
+                                  each A tile; all 512 TMEM columns), 4 stages */
 };
 
 /* Problem description. Mirrors gemm_bench::GemmProblem (reference

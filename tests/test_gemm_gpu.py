@@ -79,7 +79,7 @@ def test_alloc_operands_match_oracle_inputs(bm, orc, cuda, layout):
 
 
 # ----------------------------------------------------------------- parity
-@pytest.mark.parametrize("variant", [1, 2, 3, 4])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("layout", ["NT", "TN"])
 def test_parity_512_uniform(bm, orc, cuda, layout, variant):
     """512^3, uniform[-1,1] seed 0, full output."""
@@ -98,7 +98,7 @@ def _ktile_set(stages):
     return sorted({1, 2, stages - 1, stages, stages + 1, 3 * stages + 1} - {0})
 
 
-@pytest.mark.parametrize("variant", [1, 2, 3, 4])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("layout", ["NT", "TN"])
 def test_full_output_exact_integers(bm, orc, cuda, layout, variant):
     """tests/full_output_validation.cu:54-152 on the new kernel: M = 2 tiles,
@@ -131,7 +131,7 @@ def test_ragged_shapes(bm, orc, cuda, layout, shape):
     m, n, k = shape
     if bm.check(m, n, k, layout) != bm.BM_OK:
         pytest.skip("leading dimension not a multiple of 8 for this layout")
-    for variant in (1, 2, 3, 4):
+    for variant in (1, 2, 3, 4, 5):
         a, b, c = bm.alloc_operands(m, n, k, layout, mode=4, seed=9)
         c.fill_(float("nan"))
         _run(bm, a, b, c, layout, variant)
