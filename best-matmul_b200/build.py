@@ -56,8 +56,30 @@ def build_library(force=False, verbose=False) -> str:
     return LIB
 
 
+HARNESS_DIR = os.path.join(HERE, "build", "core")
+HARNESS_SOURCES = [os.path.join(HERE, "harness", f) for f in ("benchmark_host.cu", "full_output_validation.cu")]
+
+
+def build_harness(force=False, verbose=False) -> str:
+    """benchmark_host + full_output_validation per variant, via build.sh (manifest.tsv)."""
+    manifest = os.path.join(HARNESS_DIR, "manifest.tsv")
+    deps = _sources() + HARNESS_SOURCES + [
+        os.path.join(HERE, "kernels", "sm100_fp16_gemm.cuh"), os.path.join(HERE, "build.sh")] + [
+        os.path.join(HERE, "host", f) for f in os.listdir(os.path.join(HERE, "host"))]
+    if not force and not _stale(manifest, deps):
+        return manifest
+    res = subprocess.run(["bash", os.path.join(HERE, "build.sh"), "--suite", "core",
+                          "--with-validation"], capture_output=True, text=True)
+    if verbose or res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError("build.sh failed")
+    return manifest
+
+
 def build_all(force=False, verbose=False) -> None:
     build_library(force, verbose)
+    build_harness(force, verbose)
 
 
 if __name__ == "__main__":

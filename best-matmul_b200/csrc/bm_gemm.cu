@@ -206,10 +206,35 @@ int resolve(const bm_gemm_desc* d, Resolved* r) {
   return BM_OK;
 }
 
+// Automatic variant choice: estimated throughput = (relative per-tile
+// efficiency of the variant, measured on B200) x (fraction of the persistent
+// grid kept busy, i.e. wave quantization of the tile count over the resident
+// clusters). Skinny M (<= 128) streams B from HBM and takes the 1-CTA
+// 128x256 tile, which measured fastest there.
 int pick_variant(const bm_gemm_desc* d) {
   if (d->variant != BM_VARIANT_AUTO) return d->variant;
   if (d->m <= 128) return (d->n >= 256) ? BM_VARIANT_1CTA_128x256 : BM_VARIANT_1CTA_128x128;
-  return BM_VARIANT_2CTA_256x256;
+  static const struct { int id; double eff; } cand[] = {
+      {BM_VARIANT_2CTA_256x512, 1.00}, {BM_VARIANT_2CTA_256x256, 0.93},
+      {BM_VARIANT_1CTA_128x256, 0.88}, {BM_VARIANT_1CTA_128x128, 0.80}};
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int best = BM_VARIANT_2CTA_256x512;
+  double best_score = -1.0;
+  for (const auto& c : cand) {
+    const VariantInfo& vi = kVariants[c.id];
+    const long long tm = 128LL * vi.cta_group, tn = static_cast<long long>(vi.mma_n) * vi.num_n;
+    const long long tiles = ((d->m + tm - 1) / tm) * ((d->n + tn - 1) / tn);
+    const long long slots = sms / vi.cta_group;
+    const long long waves = (tiles + slots - 1) / slots;
+    const double busy = static_cast<double>(tiles) / static_cast<double>(waves * slots);
+    const double score = c.eff * busy;
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = c.id;
+    }
+  }
+  return best;
 }
 
 }  // namespace

@@ -135,6 +135,23 @@ struct GemmConfig {
   static_assert(kSmemBytes <= 232448, "shared memory budget (227 KB) exceeded");
 };
 
+// Epilogue ownership (shared with the host-side mapping check): epilogue warp
+// `warp` (2..9) reads TMEM lane quarter warp % 4 and, of each accumulator's
+// kChunks 32-column chunks, the half starting at epi_chunk_begin(). In chunk
+// `chunk`, step i (0..15), lane `lane` stores one 32-bit word: two consecutive
+// rows of one column of the CTA's 128-row tile.
+struct EpiCoord {
+  int row;  // first of the two rows (row, row + 1) within the CTA's 128 rows
+  int col;  // column within the tile
+};
+__host__ __device__ constexpr int epi_quarter(int warp) { return warp & 3; }
+__host__ __device__ constexpr int epi_chunk_begin(int warp, int chunks_per_warp) {
+  return ((warp - 2) / 4) * chunks_per_warp;
+}
+__host__ __device__ constexpr EpiCoord epi_word_coord(int warp, int lane, int chunk, int i) {
+  return EpiCoord{epi_quarter(warp) * 32 + (lane & ~1), chunk * 32 + 2 * i + (lane & 1)};
+}
+
 // Tile index -> (m block, n block). Tiles are walked in bands of group_m
 // M-blocks so that concurrently running CTAs share B (and A) tiles in L2.
 __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mb, int& nb) {
@@ -371,9 +388,9 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     __syncwarp();
   } else {
     // ------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
-    const int ew = warp - 2;       // epilogue warp index 0..7 (staging buffers)
-    const int chunk0 = (ew / 4) * Cfg::kChunksPerWarp;  // this warp's half of the columns
+    const int quarter = epi_quarter(warp);  // TMEM lanes [32*quarter, 32*quarter + 32)
+    const int ew = warp - 2;                // epilogue warp index 0..7 (staging buffers)
+    const int chunk0 = epi_chunk_begin(warp, Cfg::kChunksPerWarp);  // this warp's half
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tempty_leader0 = (kCtaGroup == 2) ? ptx::mapa(tempty_bar(0), 0) : tempty_bar(0);
     const uint32_t tempty_leader1 = (kCtaGroup == 2) ? ptx::mapa(tempty_bar(1), 0) : tempty_bar(1);
@@ -396,7 +413,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // store it with one TMA box. Lane pairs swap halves so that each lane
     // writes one 32-bit word holding two consecutive rows of one column:
     // column-major C, conflict-free shared-memory stores.
-    auto store_chunk = [&](const uint32_t (&r)[32], int row0, int col) {
+    auto store_chunk = [&](const uint32_t (&r)[32], int row0, int col0, int chunk) {
       const uint32_t buf =
           sEpi + static_cast<uint32_t>((ew * 2 + (chunk_count & 1)) * Cfg::kEpiBufBytes);
       ++chunk_count;
@@ -410,12 +427,15 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const float lo = __uint_as_float(odd ? recv : r[2 * i]);       // even row
         const float hi = __uint_as_float(odd ? r[2 * i + 1] : recv);   // odd row
         const __half2 h = __floats2half2_rn(lo, hi);
-        wb[(2 * i + (odd ? 1 : 0)) * 16 + (lane >> 1)] = *reinterpret_cast<const uint32_t*>(&h);
+        // the 32x32 box is column-major: 16 words (32 rows) per column
+        const EpiCoord e = epi_word_coord(warp, lane, chunk, i);
+        wb[(e.col - chunk * 32) * 16 + ((e.row - quarter * 32) >> 1)] =
+            *reinterpret_cast<const uint32_t*>(&h);
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        ptx::tma_store_2d(&tmap_c, buf, row0, col);
+        ptx::tma_store_2d(&tmap_c, buf, row0, col0 + chunk * 32);
         ptx::bulk_commit_group();
       }
     };
@@ -434,6 +454,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const int row0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * 128 + quarter * 32;
       const int col0 = nb * Cfg::kTileN;
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
+
       // Two register buffers: the TMEM load of chunk c+1 is in flight while
       // chunk c is converted and stored.
       uint32_t ra[32], rb[32];
@@ -443,7 +464,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
 #pragma unroll 1
       for (int c = chunk0; c < c_end; c += 2) {
         ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>((c + 1) * 32), rb);
-        store_chunk(ra, row0, col0 + c * 32);
+        store_chunk(ra, row0, col0, c);
         ptx::tmem_wait_ld();
         if (c + 2 < c_end) {
           ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>((c + 2) * 32), ra);
@@ -458,7 +479,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
             else ptx::mbar_arrive(tb);
           }
         }
-        store_chunk(rb, row0, col0 + (c + 1) * 32);
+        store_chunk(rb, row0, col0, c + 1);
         ptx::tmem_wait_ld();
       }
 #if defined(BM_KERNEL_STATS)
