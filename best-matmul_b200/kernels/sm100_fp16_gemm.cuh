@@ -8,9 +8,16 @@
 //
 // It is a thin C++ layer over the C ABI in include/bm_gemm.h: with_prepared()
 // calls bm_gemm_prepare once, hands the runner a zero-argument launch() that
-// only enqueues bm_gemm_launch on the measurement stream, and destroys the
-// handle when the runner returns. Failures exit non-zero, like the reference,
-// so scripts never record numbers from a failed configuration.
+// only enqueues bm_gemm_launch on the measurement stream, checks the kernel's
+// status word after the runner returns and destroys the handle. Failures exit
+// non-zero, like the reference, so scripts never record numbers from a failed
+// configuration.
+//
+// Like every GEMM_KERNEL_HEADER, it is included after the harness has declared
+// gemm_bench::GemmProblem, BenchmarkOptions, GemmBuffers and LaunchConfig; it
+// uses only their member names, so it compiles against this repository's
+// harness (host/*.hpp) and against the reference's (host/*.cuh, whose
+// GemmBuffers hold thrust::device_vector).
 //
 // Compile-time knobs (recorded in manifest.tsv by build.sh):
 //   SM100_VARIANT  0 = choose from the shape, 1..5 = a fixed bm_variant
@@ -18,10 +25,17 @@
 //                  reference's validate_problem); 0 = accept ragged shapes
 #pragma once
 
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <iostream>
 #include <type_traits>
+#include <utility>
 
 #include "../../include/bm_gemm.h"
-#include "../host/common.hpp"
 
 #ifndef SM100_VARIANT
 #define SM100_VARIANT 0
@@ -49,8 +63,26 @@ constexpr char kName[] = "sm100_tcgen05_2cta_256x512x64_s4";
 constexpr char kName[] = "sm100_tcgen05_auto";
 #endif
 
-inline bm_gemm_desc make_desc(const gemm_bench::GemmProblem& p, const void* a, const void* b,
-                              void* c) {
+namespace detail {
+
+// Device address held by a harness buffer: thrust::device_vector exposes
+// data().get(), this repository's DeviceArray exposes get().
+template <class V, class = void>
+struct has_thrust_data : std::false_type {};
+template <class V>
+struct has_thrust_data<V, std::void_t<decltype(std::declval<V&>().data().get())>> : std::true_type {};
+
+template <class V>
+void* device_pointer(V& v) {
+  if constexpr (has_thrust_data<V>::value) {
+    return static_cast<void*>(v.data().get());
+  } else {
+    return static_cast<void*>(v.get());
+  }
+}
+
+template <class Problem>
+bm_gemm_desc make_desc(const Problem& p, const void* a, const void* b, void* c) {
   bm_gemm_desc d;
   std::memset(&d, 0, sizeof(d));
   d.m = p.m;
@@ -71,35 +103,38 @@ inline bm_gemm_desc make_desc(const gemm_bench::GemmProblem& p, const void* a, c
   std::exit(EXIT_FAILURE);
 }
 
+}  // namespace detail
+
 // Shape rules of the selected kernel, checked without a GPU.
-inline void validate_problem(const gemm_bench::GemmProblem& p) {
+template <class Problem>
+void validate_problem(const Problem& p) {
   alignas(16) static char dummy[16];
-  bm_gemm_desc d = make_desc(p, dummy, dummy, dummy);
+  bm_gemm_desc d = detail::make_desc(p, dummy, dummy, dummy);
   const int rc = bm_gemm_check(&d);
   if (rc == BM_ERR_TILE_DIVISIBILITY) {
     std::cerr << "Selected kernel requires M % CTA_M == 0, N % CTA_N == 0, K % CTA_K == 0\n";
     std::exit(EXIT_FAILURE);
   }
-  if (rc != BM_OK) die("problem rejected", rc);
+  if (rc != BM_OK) detail::die("problem rejected", rc);
 }
 
 inline void print_configuration() {
   std::printf("Selected MMA: tcgen05.mma kind::f16, FP32 accumulate in TMEM (variant %d: %s)\n",
               kVariant, kName);
-  std::printf("Pipeline: TMA producer warp, single-thread MMA issuer, %d epilogue threads; "
-              "strict tile check=%d\n", 256, kStrictTiles ? 1 : 0);
+  std::printf("Pipeline: 1 TMA producer warp, 1 MMA-issuer warp, 8 epilogue warps; "
+              "strict tile check=%d\n", kStrictTiles ? 1 : 0);
 }
 
-// Prepare once, run `runner(launch, config)`, release. `launch` must not
-// outlive this call.
-template <class Runner>
-auto with_prepared(const gemm_bench::BenchmarkOptions& options,
-                             gemm_bench::GemmBuffers& buffers, const Runner& runner) {
-  bm_gemm_desc d = make_desc(options.problem, buffers.d_A.get(), buffers.d_B.get(),
-                             buffers.d_C.get());
+// Prepare once, run `runner(launch, config)`, check the kernel status, release.
+// `launch` must not outlive this call.
+template <class Options, class Buffers, class Runner>
+auto with_prepared(const Options& options, Buffers& buffers, const Runner& runner) {
+  bm_gemm_desc d = detail::make_desc(options.problem, detail::device_pointer(buffers.d_A),
+                                     detail::device_pointer(buffers.d_B),
+                                     detail::device_pointer(buffers.d_C));
   bm_gemm_handle* h = nullptr;
   const int rc = bm_gemm_prepare(&d, &h);
-  if (rc != BM_OK) die("bm_gemm_prepare", rc);
+  if (rc != BM_OK) detail::die("bm_gemm_prepare", rc);
   struct Release {
     bm_gemm_handle* h;
     ~Release() { bm_gemm_destroy(h); }
@@ -114,7 +149,7 @@ auto with_prepared(const gemm_bench::BenchmarkOptions& options,
   cudaStream_t stream = options.measurement.stream;
   auto launch = [h, stream]() {
     const int lrc = bm_gemm_launch(h, stream);
-    if (lrc != BM_OK) die("bm_gemm_launch", lrc);
+    if (lrc != BM_OK) detail::die("bm_gemm_launch", lrc);
   };
   // After the runner: every bounded wait inside the kernel must have been met.
   auto check_device = [h]() {
@@ -122,7 +157,7 @@ auto with_prepared(const gemm_bench::BenchmarkOptions& options,
     const int src = bm_gemm_status(h, &bits);
     if (src != BM_OK) {
       std::cerr << "Kernel status bits=0x" << std::hex << bits << std::dec << '\n';
-      die("bm_gemm_status", src);
+      detail::die("bm_gemm_status", src);
     }
   };
   using Result = decltype(runner(launch, config));
