@@ -86,6 +86,11 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--lib-only", action="store_true",
+                    help="build only lib/libbmgemm.so (build.sh calls this before the harness)")
     args = ap.parse_args()
-    build_all(args.force, args.verbose)
+    if args.lib_only:
+        build_library(args.force, args.verbose)
+    else:
+        build_all(args.force, args.verbose)
     print("built", LIB)

@@ -90,7 +90,7 @@ print_cmd() { printf '%q ' "$@"; printf '\n'; }
 if (( dry_run )); then
   printf '# suite=%s variants=%d with_validation=%s output=%s\n' "$suite" "${#variants[@]}" \
     "$with_validation" "$output_dir"
-  print_cmd python3 "$here/build.py"
+  print_cmd python3 "$here/build.py" --lib-only
   printf '%s\n' "$header"
   for row in "${variants[@]}"; do
     read -r id variant cg cm cn pipe mn mk infl strict <<< "$row"
@@ -103,7 +103,7 @@ fi
 
 command -v "$nvcc" >/dev/null 2>&1 || fail "CUDA compiler not found: $nvcc"
 mkdir -p -- "$output_dir"
-python3 "$here/build.py"
+python3 "$here/build.py" --lib-only
 [[ -f "$lib_dir/libbmgemm.so" ]] || fail "library build failed"
 
 # manifest is replaced atomically once every build succeeded
