@@ -70,7 +70,14 @@ struct GemmParams {
 enum StatSlot : int {
   kStatTotal = 0, kStatProdWait, kStatProdWaits, kStatMmaFullWait, kStatMmaFullWaits,
   kStatMmaTmemWait, kStatMmaTmemWaits, kStatEpiWait, kStatEpiWaits, kStatEpiBusy,
-  kStatTiles, kStatKBlocks, kStatT0, kStatT1, kStatMmaFirst, kStatMmaLast, kNumStats = 16
+  kStatTiles, kStatKBlocks, kStatT0, kStatT1, kStatMmaFirst, kStatMmaLast,
+  // per tile u < kStatUnits, %globaltimer ns: MMA start, MMA end (last commit
+  // issued), epilogue start (accumulator ready), TMEM released, epilogue end
+  // (stores issued); written by the MMA warp and epilogue warp 2 of each CTA
+  kStatUnit0 = 16, kStatUnits = 6, kStatUnitCount = kStatUnit0 + 5 * kStatUnits,
+  // set-up, %globaltimer ns (warp 1): TMEM allocated, CTA barrier, cluster barrier
+  kStatSetupAlloc, kStatSetupSync, kStatSetupCluster,
+  kNumStats
 };
 
 #if defined(BM_KERNEL_STATS)
@@ -133,6 +140,8 @@ struct GemmConfig {
   static_assert(kChunksPerWarp % 2 == 0, "each epilogue warp processes chunks in pairs");
   static_assert(kBytesA % 1024 == 0 && kBytesBPerMma % 1024 == 0, "stages keep 1 KB alignment");
   static_assert(kSmemBytes <= 232448, "shared memory budget (227 KB) exceeded");
+  static_assert(kStages * kStageBytes >= kEpiWarps * kChunksPerWarp * kEpiBufBytes,
+                "the last tile's epilogue stages every chunk in the free mainloop stages");
 };
 
 // Epilogue ownership (shared with the host-side mapping check): epilogue warp
@@ -223,14 +232,23 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     ptx::tmem_alloc<kCtaGroup>(ptx::smem_u32(tmem_slot), Cfg::kTmemCols);
     ptx::tmem_relinquish<kCtaGroup>();
   }
+#if defined(BM_KERNEL_STATS)
+  const unsigned long long g_alloc = ptx::globaltimer_ns();
+#endif
   ptx::tc_fence_before();
   __syncthreads();
+#if defined(BM_KERNEL_STATS)
+  const unsigned long long g_sync = ptx::globaltimer_ns();
+#endif
   if constexpr (kCtaGroup == 2) ptx::cluster_sync();  // peer barriers initialised
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 #if defined(BM_KERNEL_STATS)
   unsigned long long st[kNumStats] = {};
   const long long t_begin = clock64();
+  st[kStatSetupAlloc] = g_alloc;
+  st[kStatSetupSync] = g_sync;
+  st[kStatSetupCluster] = ptx::globaltimer_ns();
 #endif
 
   auto fail = [&](uint32_t bit) {
@@ -323,6 +341,10 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           break;
         }
         ptx::tc_fence_after();
+#if defined(BM_KERNEL_STATS)
+        if (st[kStatUnitCount] < kStatUnits)
+          st[kStatUnit0 + 5 * st[kStatUnitCount]] = ptx::globaltimer_ns();
+#endif
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!BM_WAIT(full_bar(stage), phase, p.timeout_ns, abort_flag, kStatMmaFullWait, kStatMmaFullWaits)) {
@@ -369,6 +391,11 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         // Accumulator complete -> both CTAs' epilogues.
         ptx::mma_commit<kCtaGroup>(tfull_bar(acc));
         if constexpr (kCtaGroup == 2) ptx::mma_commit<kCtaGroup>(ptx::mapa(tfull_bar(acc), peer));
+#if defined(BM_KERNEL_STATS)
+        if (st[kStatUnitCount] < kStatUnits)
+          st[kStatUnit0 + 5 * st[kStatUnitCount] + 1] = ptx::globaltimer_ns();
+        st[kStatUnitCount] += 1;
+#endif
         if (++acc == Cfg::kAccStages) {
           acc = 0;
           acc_phase ^= 1u;
@@ -413,24 +440,39 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // store it with one TMA box. Lane pairs swap halves so that each lane
     // writes one 32-bit word holding two consecutive rows of one column:
     // column-major C, conflict-free shared-memory stores.
-    auto store_chunk = [&](const uint32_t (&r)[32], int row0, int col0, int chunk) {
-      const uint32_t buf =
-          sEpi + static_cast<uint32_t>((ew * 2 + (chunk_count & 1)) * Cfg::kEpiBufBytes);
-      ++chunk_count;
-      if (lane == 0) ptx::bulk_wait_group_read<1>();  // buffer from 2 chunks ago is free
-      __syncwarp();
+    // Two FP32 values of one row (columns 2i, 2i+1) -> one word of FP16 pairs
+    // laid out for column-major C: lane pairs swap halves so that the even
+    // lane holds rows (lane, lane+1) of column 2i and the odd lane the same
+    // rows of column 2i+1. Each value is rounded to FP16 on its own (round to
+    // nearest even).
+    auto pack_pair = [&](uint32_t c0v, uint32_t c1v) -> uint32_t {
+      const __half2 own2 = __floats2half2_rn(__uint_as_float(c0v), __uint_as_float(c1v));
+      const uint32_t own = *reinterpret_cast<const uint32_t*>(&own2);
+      const uint32_t other = __shfl_xor_sync(0xffffffffu, own, 1);
+      return odd ? __byte_perm(other, own, 0x7632) : __byte_perm(own, other, 0x5410);
+    };
+
+    // Stage one packed 32x32 chunk in shared memory and store it with one TMA
+    // box. `big`: the CTA's last tile, whose mainloop stages are all consumed,
+    // so every chunk gets its own 2 KB of the stage area and nothing waits;
+    // otherwise two 2 KB buffers per warp alternate.
+    auto stage_store = [&](const uint32_t (&hw)[16], int row0, int col0, int chunk, bool big) {
+      uint32_t buf;
+      if (big) {
+        buf = sA + static_cast<uint32_t>((ew * Cfg::kChunksPerWarp + (chunk - chunk0)) *
+                                         Cfg::kEpiBufBytes);
+      } else {
+        buf = sEpi + static_cast<uint32_t>((ew * 2 + (chunk_count & 1)) * Cfg::kEpiBufBytes);
+        ++chunk_count;
+        if (lane == 0) ptx::bulk_wait_group_read<1>();  // buffer from 2 chunks ago is free
+        __syncwarp();
+      }
       uint32_t* wb = reinterpret_cast<uint32_t*>(smem + (buf - base));
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const uint32_t send = odd ? r[2 * i] : r[2 * i + 1];
-        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
-        const float lo = __uint_as_float(odd ? recv : r[2 * i]);       // even row
-        const float hi = __uint_as_float(odd ? r[2 * i + 1] : recv);   // odd row
-        const __half2 h = __floats2half2_rn(lo, hi);
         // the 32x32 box is column-major: 16 words (32 rows) per column
         const EpiCoord e = epi_word_coord(warp, lane, chunk, i);
-        wb[(e.col - chunk * 32) * 16 + ((e.row - quarter * 32) >> 1)] =
-            *reinterpret_cast<const uint32_t*>(&h);
+        wb[(e.col - chunk * 32) * 16 + ((e.row - quarter * 32) >> 1)] = hw[i];
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
@@ -450,41 +492,53 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       ptx::tc_fence_after();
 #if defined(BM_KERNEL_STATS)
       const long long t_epi = clock64();
+      const unsigned long long ux = st[kStatUnitCount];
+      if (ux < kStatUnits) st[kStatUnit0 + 5 * ux + 2] = ptx::globaltimer_ns();
 #endif
       const int row0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * 128 + quarter * 32;
       const int col0 = nb * Cfg::kTileN;
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
+      const bool last = tile + num_clusters >= p.num_tiles;
 
-      // Two register buffers: the TMEM load of chunk c+1 is in flight while
-      // chunk c is converted and stored.
-      uint32_t ra[32], rb[32];
-      const int c_end = chunk0 + Cfg::kChunksPerWarp;
-      ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>(chunk0 * 32), ra);
+      // Read this warp's whole share of the accumulator into registers as
+      // packed FP16 (16-column TMEM loads, double-buffered: load h+1 while
+      // packing h), hand TMEM back to the MMA issuer, then store. The stores
+      // overlap the next tile's mainloop instead of holding TMEM.
+      constexpr int kHalves = 2 * Cfg::kChunksPerWarp;
+      uint32_t hw[Cfg::kChunksPerWarp][16];
+      uint32_t ra[16], rb[16];
+      const uint32_t t_w = t_acc + static_cast<uint32_t>(chunk0 * 32);
+      ptx::tmem_ld_32x32b_x16(t_w, ra);
       ptx::tmem_wait_ld();
-#pragma unroll 1
-      for (int c = chunk0; c < c_end; c += 2) {
-        ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>((c + 1) * 32), rb);
-        store_chunk(ra, row0, col0, c);
+#pragma unroll
+      for (int h = 0; h < kHalves; h += 2) {
+        ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hw[h / 2][i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
         ptx::tmem_wait_ld();
-        if (c + 2 < c_end) {
-          ptx::tmem_ld_32x32b_x32(t_acc + static_cast<uint32_t>((c + 2) * 32), ra);
-        } else {
-          // Every TMEM read of this tile has completed: hand the
-          // accumulator back to the MMA issuer before the last stores.
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            const uint32_t tb = acc ? tempty_leader1 : tempty_leader0;
-            if constexpr (kCtaGroup == 2) ptx::mbar_arrive_cluster(tb);
-            else ptx::mbar_arrive(tb);
-          }
-        }
-        store_chunk(rb, row0, col0, c + 1);
-        ptx::tmem_wait_ld();
+        if (h + 2 < kHalves) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hw[h / 2][8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
+        if (h + 2 < kHalves) ptx::tmem_wait_ld();
       }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        const uint32_t tb = acc ? tempty_leader1 : tempty_leader0;
+        if constexpr (kCtaGroup == 2) ptx::mbar_arrive_cluster(tb);
+        else ptx::mbar_arrive(tb);
+      }
+#if defined(BM_KERNEL_STATS)
+      if (ux < kStatUnits) st[kStatUnit0 + 5 * ux + 3] = ptx::globaltimer_ns();
+#endif
+#pragma unroll
+      for (int cc = 0; cc < Cfg::kChunksPerWarp; ++cc)
+        stage_store(hw[cc], row0, col0, chunk0 + cc, last);
 #if defined(BM_KERNEL_STATS)
       st[kStatEpiBusy] += static_cast<unsigned long long>(clock64() - t_epi);
       st[kStatTiles] += 1;
+      if (ux < kStatUnits) st[kStatUnit0 + 5 * ux + 4] = ptx::globaltimer_ns();
+      st[kStatUnitCount] += 1;
 #endif
       if (++acc == Cfg::kAccStages) {
         acc = 0;
@@ -512,7 +566,20 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       out[kStatMmaTmemWait] = st[kStatMmaTmemWait];
       out[kStatMmaTmemWaits] = st[kStatMmaTmemWaits];
       out[kStatKBlocks] = st[kStatKBlocks];
+      for (int i = 0; i < kStatUnits; ++i) {
+        out[kStatUnit0 + 5 * i] = st[kStatUnit0 + 5 * i];
+        out[kStatUnit0 + 5 * i + 1] = st[kStatUnit0 + 5 * i + 1];
+      }
+      out[kStatUnitCount] = st[kStatUnitCount];
+      out[kStatSetupAlloc] = st[kStatSetupAlloc];
+      out[kStatSetupSync] = st[kStatSetupSync];
+      out[kStatSetupCluster] = st[kStatSetupCluster];
     } else if (warp == 2) {
+      for (int i = 0; i < kStatUnits; ++i) {
+        out[kStatUnit0 + 5 * i + 2] = st[kStatUnit0 + 5 * i + 2];
+        out[kStatUnit0 + 5 * i + 3] = st[kStatUnit0 + 5 * i + 3];
+        out[kStatUnit0 + 5 * i + 4] = st[kStatUnit0 + 5 * i + 4];
+      }
       out[kStatT0] = g_entry;
       out[kStatT1] = ptx::globaltimer_ns();
       out[kStatEpiWait] = st[kStatEpiWait];
