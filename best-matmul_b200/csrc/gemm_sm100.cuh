@@ -210,11 +210,53 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffTmemSlot);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + Cfg::kOffAbort);
 
+  // Origin of this CTA's part of a tile: its first A row (m0) and its first
+  // B row of MMA 0 (n0; MMA j adds j * kBN).
+  auto tile_origin = [&](int tile, int& m0, int& n0) {
+    int mb, nb;
+    tile_coords(tile, p, mb, nb);
+    m0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * Cfg::kRowsA;
+    n0 = nb * Cfg::kTileN + static_cast<int>(cta_rank) * Cfg::kRowsBPerMma;
+  };
+  // Every TMA box of one k-block for this CTA: f(is_b, byte offset in the
+  // stage's A or B part, tensor map, x, y). MN-major (NT) tiles are 64-wide
+  // boxes 8 KB apart; K-major (TN) tiles are one box per operand and MMA.
+  auto for_each_box = [&](int m0, int n0, int k0, auto&& f) {
+    if constexpr (kMnMajor) {
+      f(false, 0u, &tmap_a, m0, k0);
+      f(false, 8192u, &tmap_a, m0 + 64, k0);
+#pragma unroll
+      for (int j = 0; j < kNumN; ++j)
+#pragma unroll
+        for (int q = 0; q < Cfg::kRowsBPerMma / 64; ++q)
+          f(true, static_cast<uint32_t>(j * Cfg::kBytesBPerMma + 8192 * q), &tmap_b,
+            n0 + j * kBN + 64 * q, k0);
+    } else {
+      f(false, 0u, &tmap_a, k0, m0);
+#pragma unroll
+      for (int j = 0; j < kNumN; ++j)
+        f(true, static_cast<uint32_t>(j * Cfg::kBytesBPerMma), &tmap_b, k0, n0 + j * kBN);
+    }
+  };
+
   // ------------------------------------------------------------ set-up
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&tmap_a);
     ptx::prefetch_tmap(&tmap_b);
     ptx::prefetch_tmap(&tmap_c);
+    // Start pulling the first tile's first k-blocks into L2 now: the DRAM
+    // latency then overlaps barrier/TMEM set-up and the pair's cluster
+    // barrier instead of following them.
+    if (cluster_id < p.num_tiles) {
+      int m0, n0;
+      tile_origin(cluster_id, m0, n0);
+      const int npf = p.k_blocks < kStages ? p.k_blocks : kStages;
+      for (int kb = 0; kb < npf; ++kb)
+        for_each_box(m0, n0, kb * Cfg::kBK,
+                     [&](bool, uint32_t, const CUtensorMap* map, int x, int y) {
+                       ptx::tma_prefetch_2d(map, x, y);
+                     });
+    }
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(full_bar(s), 1);   // the (leader) producer's arrive.expect_tx
       ptx::mbar_init(empty_bar(s), 1);  // one tcgen05.commit per use
@@ -263,11 +305,8 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters) {
-        int mb, nb;
-        tile_coords(tile, p, mb, nb);
-        const int m0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * Cfg::kRowsA;
-        // this CTA's B rows for MMA j: nb*kTileN + j*kBN + rank*kRowsBPerMma + [0, kRowsBPerMma)
-        const int n0 = nb * Cfg::kTileN + static_cast<int>(cta_rank) * Cfg::kRowsBPerMma;
+        int m0, n0;
+        tile_origin(tile, m0, n0);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!BM_WAIT(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, kStatProdWait, kStatProdWaits)) {
             fail(kStatusProducerTimeout);
@@ -287,24 +326,11 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
             fb = ptx::mapa(full_bar(stage), 0);
             if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * Cfg::kStageBytes);
           }
-          auto load = [&](uint32_t dst, const CUtensorMap* map, int x, int y) {
+          for_each_box(m0, n0, k0, [&](bool is_b, uint32_t off, const CUtensorMap* map, int x, int y) {
+            const uint32_t dst = (is_b ? b_dst : a_dst) + off;
             if constexpr (kCtaGroup == 1) ptx::tma_load_2d(dst, map, fb, x, y);
             else ptx::tma_load_2d_pair(dst, map, fb, x, y);
-          };
-          if constexpr (kMnMajor) {
-            load(a_dst, &tmap_a, m0, k0);
-            load(a_dst + 8192, &tmap_a, m0 + 64, k0);
-#pragma unroll
-            for (int j = 0; j < kNumN; ++j)
-#pragma unroll
-              for (int q = 0; q < Cfg::kRowsBPerMma / 64; ++q)
-                load(b_dst + j * Cfg::kBytesBPerMma + 8192 * q, &tmap_b, n0 + j * kBN + 64 * q, k0);
-          } else {
-            load(a_dst, &tmap_a, k0, m0);
-#pragma unroll
-            for (int j = 0; j < kNumN; ++j)
-              load(b_dst + j * Cfg::kBytesBPerMma, &tmap_b, k0, n0 + j * kBN);
-          }
+          });
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
