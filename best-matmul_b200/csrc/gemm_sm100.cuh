@@ -71,10 +71,13 @@ enum StatSlot : int {
   kStatTotal = 0, kStatProdWait, kStatProdWaits, kStatMmaFullWait, kStatMmaFullWaits,
   kStatMmaTmemWait, kStatMmaTmemWaits, kStatEpiWait, kStatEpiWaits, kStatEpiBusy,
   kStatTiles, kStatKBlocks, kStatT0, kStatT1, kStatMmaFirst, kStatMmaLast,
-  // per tile u < kStatUnits, %globaltimer ns: MMA start, MMA end (last commit
-  // issued), epilogue start (accumulator ready), TMEM released, epilogue end
-  // (stores issued); written by the MMA warp and epilogue warp 2 of each CTA
-  kStatUnit0 = 16, kStatUnits = 6, kStatUnitCount = kStatUnit0 + 5 * kStatUnits,
+  // per tile u < kStatUnits (kStatUnitFields slots each), %globaltimer ns:
+  // MMA start, MMA end (last commit issued), epilogue start (accumulator
+  // ready), TMEM released, epilogue end (stores issued); then the MMA
+  // thread's cycles waiting for loaded stages during the tile. Written
+  // straight to global memory by the MMA thread and epilogue warp 2.
+  kStatUnit0 = 16, kStatUnits = 6, kStatUnitFields = 6,
+  kStatUnitCount = kStatUnit0 + kStatUnitFields * kStatUnits,
   // set-up, %globaltimer ns (warp 1): TMEM allocated, CTA barrier, cluster barrier
   kStatSetupAlloc, kStatSetupSync, kStatSetupCluster,
   kNumStats
@@ -92,6 +95,8 @@ __device__ __forceinline__ bool stat_wait(uint32_t bar, uint32_t parity, uint64_
   return ok;
 }
 #define BM_WAIT(bar, par, to, ab, CYC, CNT) stat_wait(bar, par, to, ab, st[CYC], st[CNT])
+#define BM_STAT_PUT(slot, v) \
+  do { if (p.stats) p.stats[static_cast<size_t>(blockIdx.x) * kNumStats + (slot)] = (v); } while (0)
 #else
 #define BM_WAIT(bar, par, to, ab, CYC, CNT) ptx::bm_wait(bar, par, to, ab)
 #endif
@@ -244,19 +249,6 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     ptx::prefetch_tmap(&tmap_a);
     ptx::prefetch_tmap(&tmap_b);
     ptx::prefetch_tmap(&tmap_c);
-    // Start pulling the first tile's first k-blocks into L2 now: the DRAM
-    // latency then overlaps barrier/TMEM set-up and the pair's cluster
-    // barrier instead of following them.
-    if (cluster_id < p.num_tiles) {
-      int m0, n0;
-      tile_origin(cluster_id, m0, n0);
-      const int npf = p.k_blocks < kStages ? p.k_blocks : kStages;
-      for (int kb = 0; kb < npf; ++kb)
-        for_each_box(m0, n0, kb * Cfg::kBK,
-                     [&](bool, uint32_t, const CUtensorMap* map, int x, int y) {
-                       ptx::tma_prefetch_2d(map, x, y);
-                     });
-    }
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(full_bar(s), 1);   // the (leader) producer's arrive.expect_tx
       ptx::mbar_init(empty_bar(s), 1);  // one tcgen05.commit per use
@@ -286,11 +278,15 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 #if defined(BM_KERNEL_STATS)
-  unsigned long long st[kNumStats] = {};
+  unsigned long long st[kNumStats] = {};  // constant indices only: registers
   const long long t_begin = clock64();
-  st[kStatSetupAlloc] = g_alloc;
-  st[kStatSetupSync] = g_sync;
-  st[kStatSetupCluster] = ptx::globaltimer_ns();
+  if (warp == 1 && lane == 0) {
+    BM_STAT_PUT(kStatSetupAlloc, g_alloc);
+    BM_STAT_PUT(kStatSetupSync, g_sync);
+    BM_STAT_PUT(kStatSetupCluster, ptx::globaltimer_ns());
+  }
+  int unit_i = 0;
+  unsigned long long unit_wait0 = 0;
 #endif
 
   auto fail = [&](uint32_t bit) {
@@ -368,8 +364,8 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
         ptx::tc_fence_after();
 #if defined(BM_KERNEL_STATS)
-        if (st[kStatUnitCount] < kStatUnits)
-          st[kStatUnit0 + 5 * st[kStatUnitCount]] = ptx::globaltimer_ns();
+        if (unit_i < kStatUnits) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i, ptx::globaltimer_ns());
+        unit_wait0 = st[kStatMmaFullWait];
 #endif
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -418,9 +414,12 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         ptx::mma_commit<kCtaGroup>(tfull_bar(acc));
         if constexpr (kCtaGroup == 2) ptx::mma_commit<kCtaGroup>(ptx::mapa(tfull_bar(acc), peer));
 #if defined(BM_KERNEL_STATS)
-        if (st[kStatUnitCount] < kStatUnits)
-          st[kStatUnit0 + 5 * st[kStatUnitCount] + 1] = ptx::globaltimer_ns();
-        st[kStatUnitCount] += 1;
+        if (unit_i < kStatUnits) {
+          BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 1, ptx::globaltimer_ns());
+          BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 5, st[kStatMmaFullWait] - unit_wait0);
+        }
+        ++unit_i;
+        BM_STAT_PUT(kStatUnitCount, static_cast<unsigned long long>(unit_i));
 #endif
         if (++acc == Cfg::kAccStages) {
           acc = 0;
@@ -518,8 +517,8 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       ptx::tc_fence_after();
 #if defined(BM_KERNEL_STATS)
       const long long t_epi = clock64();
-      const unsigned long long ux = st[kStatUnitCount];
-      if (ux < kStatUnits) st[kStatUnit0 + 5 * ux + 2] = ptx::globaltimer_ns();
+      const bool put = warp == 2 && lane == 0 && unit_i < kStatUnits;
+      if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 2, ptx::globaltimer_ns());
 #endif
       const int row0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * 128 + quarter * 32;
       const int col0 = nb * Cfg::kTileN;
@@ -555,7 +554,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         else ptx::mbar_arrive(tb);
       }
 #if defined(BM_KERNEL_STATS)
-      if (ux < kStatUnits) st[kStatUnit0 + 5 * ux + 3] = ptx::globaltimer_ns();
+      if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 3, ptx::globaltimer_ns());
 #endif
 #pragma unroll
       for (int cc = 0; cc < Cfg::kChunksPerWarp; ++cc)
@@ -563,8 +562,8 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
 #if defined(BM_KERNEL_STATS)
       st[kStatEpiBusy] += static_cast<unsigned long long>(clock64() - t_epi);
       st[kStatTiles] += 1;
-      if (ux < kStatUnits) st[kStatUnit0 + 5 * ux + 4] = ptx::globaltimer_ns();
-      st[kStatUnitCount] += 1;
+      if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 4, ptx::globaltimer_ns());
+      ++unit_i;
 #endif
       if (++acc == Cfg::kAccStages) {
         acc = 0;
@@ -592,20 +591,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       out[kStatMmaTmemWait] = st[kStatMmaTmemWait];
       out[kStatMmaTmemWaits] = st[kStatMmaTmemWaits];
       out[kStatKBlocks] = st[kStatKBlocks];
-      for (int i = 0; i < kStatUnits; ++i) {
-        out[kStatUnit0 + 5 * i] = st[kStatUnit0 + 5 * i];
-        out[kStatUnit0 + 5 * i + 1] = st[kStatUnit0 + 5 * i + 1];
-      }
-      out[kStatUnitCount] = st[kStatUnitCount];
-      out[kStatSetupAlloc] = st[kStatSetupAlloc];
-      out[kStatSetupSync] = st[kStatSetupSync];
-      out[kStatSetupCluster] = st[kStatSetupCluster];
     } else if (warp == 2) {
-      for (int i = 0; i < kStatUnits; ++i) {
-        out[kStatUnit0 + 5 * i + 2] = st[kStatUnit0 + 5 * i + 2];
-        out[kStatUnit0 + 5 * i + 3] = st[kStatUnit0 + 5 * i + 3];
-        out[kStatUnit0 + 5 * i + 4] = st[kStatUnit0 + 5 * i + 4];
-      }
       out[kStatT0] = g_entry;
       out[kStatT1] = ptx::globaltimer_ns();
       out[kStatEpiWait] = st[kStatEpiWait];
