@@ -525,40 +525,68 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
       const bool last = tile + num_clusters >= p.num_tiles;
 
-      // Read this warp's whole share of the accumulator into registers as
-      // packed FP16 (16-column TMEM loads, double-buffered: load h+1 while
-      // packing h), hand TMEM back to the MMA issuer, then store. The stores
-      // overlap the next tile's mainloop instead of holding TMEM.
       constexpr int kHalves = 2 * Cfg::kChunksPerWarp;
-      uint32_t hw[Cfg::kChunksPerWarp][16];
-      uint32_t ra[16], rb[16];
       const uint32_t t_w = t_acc + static_cast<uint32_t>(chunk0 * 32);
-      ptx::tmem_ld_32x32b_x16(t_w, ra);
-      ptx::tmem_wait_ld();
-#pragma unroll
-      for (int h = 0; h < kHalves; h += 2) {
-        ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hw[h / 2][i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
-        ptx::tmem_wait_ld();
-        if (h + 2 < kHalves) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hw[h / 2][8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
-        if (h + 2 < kHalves) ptx::tmem_wait_ld();
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        const uint32_t tb = acc ? tempty_leader1 : tempty_leader0;
-        if constexpr (kCtaGroup == 2) ptx::mbar_arrive_cluster(tb);
-        else ptx::mbar_arrive(tb);
-      }
+      // Hand the accumulator back to the MMA issuer once every TMEM read of
+      // this warp has completed.
+      auto release_tmem = [&]() {
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t tb = acc ? tempty_leader1 : tempty_leader0;
+          if constexpr (kCtaGroup == 2) ptx::mbar_arrive_cluster(tb);
+          else ptx::mbar_arrive(tb);
+        }
 #if defined(BM_KERNEL_STATS)
-      if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 3, ptx::globaltimer_ns());
+        if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 3, ptx::globaltimer_ns());
 #endif
+      };
+      if (last) {
+        // No next tile waits for TMEM: store each chunk as soon as it is
+        // packed, so TMEM reads and stores overlap (16-column TMEM loads,
+        // double-buffered).
+        uint32_t ra[16], rb[16];
+        ptx::tmem_ld_32x32b_x16(t_w, ra);
+        ptx::tmem_wait_ld();
+#pragma unroll 1
+        for (int h = 0; h < kHalves; h += 2) {
+          uint32_t hc[16];
+          ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
 #pragma unroll
-      for (int cc = 0; cc < Cfg::kChunksPerWarp; ++cc)
-        stage_store(hw[cc], row0, col0, chunk0 + cc, last);
+          for (int i = 0; i < 8; ++i) hc[i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
+          ptx::tmem_wait_ld();
+          if (h + 2 < kHalves) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) hc[8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
+          stage_store(hc, row0, col0, chunk0 + h / 2, true);
+          if (h + 2 < kHalves) ptx::tmem_wait_ld();
+        }
+        release_tmem();
+      } else {
+        // Read this warp's whole share of the accumulator into registers as
+        // packed FP16 (load h+1 while packing h), hand TMEM back to the MMA
+        // issuer, then store: the stores overlap the next tile's mainloop
+        // instead of holding TMEM.
+        uint32_t hw[Cfg::kChunksPerWarp][16];
+        uint32_t ra[16], rb[16];
+        ptx::tmem_ld_32x32b_x16(t_w, ra);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < kHalves; h += 2) {
+          ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) hw[h / 2][i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
+          ptx::tmem_wait_ld();
+          if (h + 2 < kHalves) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) hw[h / 2][8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
+          if (h + 2 < kHalves) ptx::tmem_wait_ld();
+        }
+        release_tmem();
+#pragma unroll
+        for (int cc = 0; cc < Cfg::kChunksPerWarp; ++cc)
+          stage_store(hw[cc], row0, col0, chunk0 + cc, false);
+      }
 #if defined(BM_KERNEL_STATS)
       st[kStatEpiBusy] += static_cast<unsigned long long>(clock64() - t_epi);
       st[kStatTiles] += 1;
