@@ -48,6 +48,9 @@ VARIANT_TILES = {1: (256, 256, 6), 2: (128, 256, 4), 3: (128, 128, 6), 4: (256, 
 
 DEBUG_EPILOGUE_WAITS_NEVER = 1
 
+SPLIT_NONE = 0
+SPLIT_AUTO = 1
+
 
 class BmGemmError(RuntimeError):
     def __init__(self, code: int, what: str = ""):
@@ -69,6 +72,15 @@ class GemmDesc(ctypes.Structure):
         ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("c", ctypes.c_void_p),
         ("lda", ctypes.c_int64), ("ldb", ctypes.c_int64), ("ldc", ctypes.c_int64),
         ("variant", ctypes.c_int), ("strict_tiles", ctypes.c_int),
+    ]
+
+
+class ScheduleInfo(ctypes.Structure):
+    _fields_ = [
+        ("whole_tiles", ctypes.c_int), ("split_tiles", ctypes.c_int),
+        ("split_quarters", ctypes.c_int), ("split_clusters", ctypes.c_int),
+        ("grid_clusters", ctypes.c_int), ("resident_clusters", ctypes.c_int),
+        ("quarter_cols", ctypes.c_int),
     ]
 
 
@@ -112,6 +124,10 @@ def load() -> ctypes.CDLL:
     lib.bm_gemm_status.argtypes = [vp, ctypes.POINTER(u32)]
     lib.bm_gemm_set_debug.restype = i32
     lib.bm_gemm_set_debug.argtypes = [vp, u64, u32]
+    lib.bm_gemm_set_split.restype = i32
+    lib.bm_gemm_set_split.argtypes = [vp, i32]
+    lib.bm_gemm_query_schedule.restype = i32
+    lib.bm_gemm_query_schedule.argtypes = [vp, ctypes.POINTER(ScheduleInfo)]
     lib.bm_gemm_destroy.restype = None
     lib.bm_gemm_destroy.argtypes = [vp]
     lib.bm_fill_fp16.restype = i32
@@ -222,6 +238,19 @@ class Gemm:
             "name": variant_name(li.variant), "tile": (li.tile_m, li.tile_n, li.tile_k),
             "stages": li.stages, "num_tiles": li.num_tiles, "cta_group": li.cta_group,
         }
+
+    def set_split(self, mode: int) -> None:
+        """bm_gemm_set_split: SPLIT_AUTO (default) or SPLIT_NONE."""
+        rc = self._lib.bm_gemm_set_split(self._h, mode)
+        if rc != BM_OK:
+            raise BmGemmError(rc, "bm_gemm_set_split")
+
+    def schedule(self) -> dict:
+        si = ScheduleInfo()
+        rc = self._lib.bm_gemm_query_schedule(self._h, ctypes.byref(si))
+        if rc != BM_OK:
+            raise BmGemmError(rc, "bm_gemm_query_schedule")
+        return {f: getattr(si, f) for f, _ in ScheduleInfo._fields_}
 
     def status(self) -> tuple[int, int]:
         """(return code, device status bits); synchronises the device."""

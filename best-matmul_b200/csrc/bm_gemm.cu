@@ -21,6 +21,7 @@
 #include "../../include/bm_gemm.h"
 #include "bm_inputs.cuh"
 #include "gemm_sm100.cuh"
+#include "schedule.cuh"
 
 namespace {
 
@@ -74,6 +75,9 @@ struct bm_gemm_handle {
   int device;
   uint32_t* d_status;
   LaunchFn launch;
+  int max_clusters;  // resident clusters of this variant on this device
+  int quarters;      // column quarters per tile the variant can split into (1: none)
+  int split_mode;    // enum bm_split_mode
 };
 
 namespace {
@@ -206,6 +210,24 @@ int resolve(const bm_gemm_desc* d, Resolved* r) {
   return BM_OK;
 }
 
+// Column quarters a variant's leftover tiles can be split into (1 = whole
+// tiles only): the 256x512 pair tile (GemmConfig::kTailSplit).
+int split_quarters(int variant) {
+  const VariantInfo& vi = kVariants[variant];
+  return (vi.cta_group == 2 && vi.mma_n == 256 && vi.num_n == 2) ? (vi.mma_n * vi.num_n) / bm::kQuarterCols
+                                                                   : 1;
+}
+
+void apply_plan(bm_gemm_handle* h) {
+  GemmParams& p = h->params;
+  const bm::Plan pl = bm::plan_schedule(p.num_tiles, h->quarters, h->max_clusters,
+                                        h->split_mode == BM_SPLIT_AUTO ? 1 : 0);
+  p.dp_tiles = pl.dp_tiles;
+  p.tail_quarters = pl.tail_quarters;
+  p.tail_clusters = pl.tail_clusters;
+  h->grid = pl.grid_clusters * h->cta_group;
+}
+
 // Automatic variant choice: estimated throughput = (relative per-tile
 // efficiency of the variant, measured on B200) x (fraction of the persistent
 // grid kept busy, i.e. wave quantization of the tile count over the resident
@@ -225,9 +247,10 @@ int pick_variant(const bm_gemm_desc* d) {
     const VariantInfo& vi = kVariants[c.id];
     const long long tm = 128LL * vi.cta_group, tn = static_cast<long long>(vi.mma_n) * vi.num_n;
     const long long tiles = ((d->m + tm - 1) / tm) * ((d->n + tn - 1) / tn);
-    const long long slots = sms / vi.cta_group;
-    const long long waves = (tiles + slots - 1) / slots;
-    const double busy = static_cast<double>(tiles) / static_cast<double>(waves * slots);
+    const int slots = sms / vi.cta_group;
+    // waves as scheduled (leftover tiles split into quarters where possible)
+    const bm::Plan pl = bm::plan_schedule(static_cast<int>(tiles), split_quarters(c.id), slots, 1);
+    const double busy = static_cast<double>(tiles) / (static_cast<double>(slots) * pl.est);
     const double score = c.eff * busy;
     if (score > best_score + 1e-9) {
       best_score = score;
@@ -360,8 +383,10 @@ int bm_gemm_prepare(const bm_gemm_desc* d, bm_gemm_handle** out) {
   p.timeout_ns = kDefaultTimeoutNs;
   p.debug = 0;
   p.stats = nullptr;
-  const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
-  h->grid = clusters * h->cta_group;
+  h->max_clusters = max_clusters;
+  h->quarters = split_quarters(v);
+  h->split_mode = BM_SPLIT_AUTO;
+  apply_plan(h);
 
   if (cudaMalloc(reinterpret_cast<void**>(&h->d_status), sizeof(uint32_t)) != cudaSuccess) {
     delete h;
@@ -418,6 +443,27 @@ int bm_gemm_set_debug(bm_gemm_handle* h, uint64_t timeout_ns, uint32_t flags) {
   if (!h || timeout_ns == 0) return BM_ERR_INVALID_ARGUMENT;
   h->params.timeout_ns = timeout_ns;
   h->params.debug = flags;
+  return BM_OK;
+}
+
+int bm_gemm_set_split(bm_gemm_handle* h, int mode) {
+  if (!h || (mode != BM_SPLIT_NONE && mode != BM_SPLIT_AUTO)) return BM_ERR_INVALID_ARGUMENT;
+  h->split_mode = mode;
+  apply_plan(h);
+  return BM_OK;
+}
+
+int bm_gemm_query_schedule(const bm_gemm_handle* h, bm_schedule_info* info) {
+  if (!h || !info) return BM_ERR_INVALID_ARGUMENT;
+  std::memset(info, 0, sizeof(*info));
+  const GemmParams& p = h->params;
+  info->whole_tiles = p.dp_tiles;
+  info->split_tiles = p.num_tiles - p.dp_tiles;
+  info->split_quarters = p.tail_quarters;
+  info->split_clusters = p.tail_clusters;
+  info->grid_clusters = h->grid / h->cta_group;
+  info->resident_clusters = h->max_clusters;
+  info->quarter_cols = h->quarters > 1 ? bm::kQuarterCols : 0;
   return BM_OK;
 }
 
@@ -593,6 +639,9 @@ extern "C" int bm_gemm_run_noalloc(const bm_gemm_desc* d, void* stream, uint32_t
   p.debug = 0;
   p.stats = nullptr;
   p.status = nd.scratch;
+  p.dp_tiles = p.num_tiles;  // whole tiles, one wave after another
+  p.tail_quarters = 0;
+  p.tail_clusters = 0;
   const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
   h.grid = clusters * h.cta_group;
 

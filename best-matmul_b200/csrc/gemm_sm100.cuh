@@ -35,6 +35,7 @@
 
 #include <cuda_fp16.h>
 #include "ptx_sm100.cuh"
+#include "schedule.cuh"
 
 namespace bm {
 
@@ -62,6 +63,13 @@ struct GemmParams {
   uint64_t timeout_ns;   // bound on every mbarrier wait
   uint32_t debug;        // kDebug* flags; 0 in production
   unsigned long long* stats;  // per-CTA cycle counters; only read in BM_KERNEL_STATS builds
+  // Schedule (schedule.cuh): tiles [0, dp_tiles) whole, cluster c taking c,
+  // c + clusters, ...; then the column quarters of tiles [dp_tiles,
+  // num_tiles) split over clusters [0, tail_clusters) (tail_quarters = 0:
+  // nothing split).
+  int dp_tiles;
+  int tail_quarters;
+  int tail_clusters;
 };
 
 // Opt-in pipeline counters (build with -DBM_KERNEL_STATS): per CTA, cycles
@@ -136,6 +144,11 @@ struct GemmConfig {
   static constexpr int kOffAbort = kOffTmemSlot + 4;
   static constexpr int kSmemBytes = kOffAbort + 4 + 1024;  // + alignment slack
   static constexpr uint32_t kIdesc = make_idesc_f16_f32(kMmaM, kBN, kMnMajor);
+  // Column quarters per tile, and whether leftover tiles may be computed in
+  // quarter runs (the 256x512 pair tile: runs of 128..512 columns map onto
+  // one or two MMAs of N = 128 or 256, B rows per CTA stay multiples of 64).
+  static constexpr int kQuarters = kTileN / kQuarterCols;
+  static constexpr bool kTailSplit = (kCtaGroup == 2 && kNumN == 2 && kBN == 256);
 
   static_assert(kBN == 128 || kBN == 256, "kBN must be 128 or 256");
   static_assert(kNumN == 1 || kNumN == 2, "kNumN must be 1 or 2");
@@ -165,6 +178,11 @@ __host__ __device__ constexpr int epi_chunk_begin(int warp, int chunks_per_warp)
 __host__ __device__ constexpr EpiCoord epi_word_coord(int warp, int lane, int chunk, int i) {
   return EpiCoord{epi_quarter(warp) * 32 + (lane & ~1), chunk * 32 + 2 * i + (lane & 1)};
 }
+
+template <int N>
+struct IntTag {
+  static constexpr int value = N;
+};
 
 // Tile index -> (m block, n block). Tiles are walked in bands of group_m
 // M-blocks so that concurrently running CTAs share B (and A) tiles in L2.
@@ -214,35 +232,6 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
   const uint32_t never_bar = bar0 + 8u * (2 * kStages + 5);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffTmemSlot);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(smem + Cfg::kOffAbort);
-
-  // Origin of this CTA's part of a tile: its first A row (m0) and its first
-  // B row of MMA 0 (n0; MMA j adds j * kBN).
-  auto tile_origin = [&](int tile, int& m0, int& n0) {
-    int mb, nb;
-    tile_coords(tile, p, mb, nb);
-    m0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * Cfg::kRowsA;
-    n0 = nb * Cfg::kTileN + static_cast<int>(cta_rank) * Cfg::kRowsBPerMma;
-  };
-  // Every TMA box of one k-block for this CTA: f(is_b, byte offset in the
-  // stage's A or B part, tensor map, x, y). MN-major (NT) tiles are 64-wide
-  // boxes 8 KB apart; K-major (TN) tiles are one box per operand and MMA.
-  auto for_each_box = [&](int m0, int n0, int k0, auto&& f) {
-    if constexpr (kMnMajor) {
-      f(false, 0u, &tmap_a, m0, k0);
-      f(false, 8192u, &tmap_a, m0 + 64, k0);
-#pragma unroll
-      for (int j = 0; j < kNumN; ++j)
-#pragma unroll
-        for (int q = 0; q < Cfg::kRowsBPerMma / 64; ++q)
-          f(true, static_cast<uint32_t>(j * Cfg::kBytesBPerMma + 8192 * q), &tmap_b,
-            n0 + j * kBN + 64 * q, k0);
-    } else {
-      f(false, 0u, &tmap_a, k0, m0);
-#pragma unroll
-      for (int j = 0; j < kNumN; ++j)
-        f(true, static_cast<uint32_t>(j * Cfg::kBytesBPerMma), &tmap_b, k0, n0 + j * kBN);
-    }
-  };
 
   // ------------------------------------------------------------ set-up
   if (warp == 0 && lane == 0) {
@@ -300,9 +289,27 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters) {
-        int m0, n0;
-        tile_origin(tile, m0, n0);
+      WorkIter<Cfg::kQuarters> it(p, cluster_id, num_clusters);
+      WorkUnit u;
+      while (ok && it.next(p, u)) {
+        int mb, nb;
+        tile_coords(u.tile, p, mb, nb);
+        // Columns of this unit: n_unit from nbase; MMA j covers
+        // [nbase + j*kBN, + nj), nj = min(n_unit - j*kBN, kBN) (<= 0: no MMA j),
+        // and this CTA holds B rows [rank * nj / kCtaGroup, + nj / kCtaGroup).
+        const int n_unit = Cfg::kTailSplit ? u.w * kQuarterCols : Cfg::kTileN;
+        const int nbase = nb * Cfg::kTileN + (Cfg::kTailSplit ? u.q0 * kQuarterCols : 0);
+        const int m0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * Cfg::kRowsA;
+        // Bytes this CTA lands per stage. K-major B loads whole boxes of
+        // kRowsBPerMma rows even when a narrower MMA uses only the first half.
+        uint32_t stage_bytes = Cfg::kBytesA;
+#pragma unroll
+        for (int j = 0; j < kNumN; ++j) {
+          const int nj = min(n_unit - j * kBN, kBN);
+          if (nj > 0)
+            stage_bytes += kMnMajor ? static_cast<uint32_t>(nj / kCtaGroup) * (Cfg::kBK * 2)
+                                    : static_cast<uint32_t>(Cfg::kBytesBPerMma);
+        }
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!BM_WAIT(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, kStatProdWait, kStatProdWaits)) {
             fail(kStatusProducerTimeout);
@@ -317,16 +324,38 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           uint32_t fb;
           if constexpr (kCtaGroup == 1) {
             fb = full_bar(stage);
-            ptx::mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+            ptx::mbar_arrive_expect_tx(fb, stage_bytes);
           } else {
             fb = ptx::mapa(full_bar(stage), 0);
-            if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * Cfg::kStageBytes);
+            if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * stage_bytes);
           }
-          for_each_box(m0, n0, k0, [&](bool is_b, uint32_t off, const CUtensorMap* map, int x, int y) {
-            const uint32_t dst = (is_b ? b_dst : a_dst) + off;
+          auto load = [&](uint32_t dst, const CUtensorMap* map, int x, int y) {
             if constexpr (kCtaGroup == 1) ptx::tma_load_2d(dst, map, fb, x, y);
             else ptx::tma_load_2d_pair(dst, map, fb, x, y);
-          });
+          };
+          // MN-major (NT) tiles are 64-wide boxes 8 KB apart; K-major (TN)
+          // tiles are one box per operand and MMA.
+          if constexpr (kMnMajor) {
+            load(a_dst, &tmap_a, m0, k0);
+            load(a_dst + 8192, &tmap_a, m0 + 64, k0);
+          } else {
+            load(a_dst, &tmap_a, k0, m0);
+          }
+#pragma unroll
+          for (int j = 0; j < kNumN; ++j) {
+            const int nj = min(n_unit - j * kBN, kBN);
+            if (nj <= 0) break;
+            const int rows = nj / kCtaGroup;
+            const int r0 = nbase + j * kBN + static_cast<int>(cta_rank) * rows;
+            const uint32_t dst = b_dst + j * Cfg::kBytesBPerMma;
+            if constexpr (kMnMajor) {
+#pragma unroll
+              for (int q = 0; q < Cfg::kRowsBPerMma / 64; ++q)
+                if (64 * q < rows) load(dst + 8192 * q, &tmap_b, r0 + 64 * q, k0);
+            } else {
+              load(dst, &tmap_b, k0, r0);
+            }
+          }
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -357,7 +386,17 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t acc_phase = 0;
       bool ok = true;
       const uint32_t peer = 1u;
-      for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters) {
+      WorkIter<Cfg::kQuarters> it(p, cluster_id, num_clusters);
+      WorkUnit u;
+      while (ok && it.next(p, u)) {
+        // N of MMA j for this unit (whole tiles: kBN each, compile-time).
+        const int n_unit = Cfg::kTailSplit ? u.w * kQuarterCols : Cfg::kTileN;
+        const int n0 = Cfg::kTailSplit ? min(n_unit, kBN) : kBN;
+        const int n1 = Cfg::kTailSplit ? n_unit - kBN : kBN;
+        const uint32_t idesc0 = Cfg::kTailSplit ? make_idesc_f16_f32(Cfg::kMmaM, n0, kMnMajor) : Cfg::kIdesc;
+        const uint32_t idesc1 =
+            Cfg::kTailSplit ? make_idesc_f16_f32(Cfg::kMmaM, n1 > 0 ? n1 : kBN, kMnMajor) : Cfg::kIdesc;
+        const int n_mma = (kNumN == 2 && n1 > 0) ? 2 : 1;
         if (!BM_WAIT(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns, abort_flag, kStatMmaTmemWait, kStatMmaTmemWaits)) {
           fail(kStatusMmaTimeout);
           break;
@@ -389,13 +428,14 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint64_t a_desc = ptx::smem_desc_sw128(a_base + koff, lbo, 1024);
 #pragma unroll
             for (int j = 0; j < kNumN; ++j) {
+              if (j >= n_mma) break;
               const uint64_t b_desc =
                   ptx::smem_desc_sw128(b_base + j * Cfg::kBytesBPerMma + koff, lbo, 1024);
 #if defined(BM_KERNEL_STATS)
               if (st[kStatMmaFirst] == 0) st[kStatMmaFirst] = ptx::globaltimer_ns();
 #endif
               ptx::mma_f16<kCtaGroup>(d_tmem + static_cast<uint32_t>(j * kBN), a_desc, b_desc,
-                                      Cfg::kIdesc, (kb > 0 || ks > 0) ? 1u : 0u);
+                                      j == 0 ? idesc0 : idesc1, (kb > 0 || ks > 0) ? 1u : 0u);
             }
           }
           // Free this stage in every CTA that loaded into it.
@@ -442,7 +482,6 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // ------------------------------------------------------ epilogue
     const int quarter = epi_quarter(warp);  // TMEM lanes [32*quarter, 32*quarter + 32)
     const int ew = warp - 2;                // epilogue warp index 0..7 (staging buffers)
-    const int chunk0 = epi_chunk_begin(warp, Cfg::kChunksPerWarp);  // this warp's half
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tempty_leader0 = (kCtaGroup == 2) ? ptx::mapa(tempty_bar(0), 0) : tempty_bar(0);
     const uint32_t tempty_leader1 = (kCtaGroup == 2) ? ptx::mapa(tempty_bar(1), 0) : tempty_bar(1);
@@ -478,14 +517,15 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
     };
 
     // Stage one packed 32x32 chunk in shared memory and store it with one TMA
-    // box. `big`: the CTA's last tile, whose mainloop stages are all consumed,
-    // so every chunk gets its own 2 KB of the stage area and nothing waits;
-    // otherwise two 2 KB buffers per warp alternate.
-    auto stage_store = [&](const uint32_t (&hw)[16], int row0, int col0, int chunk, bool big) {
+    // box. `big`: the CTA's last unit, whose mainloop stages are all consumed,
+    // so every chunk of the warp (index `slot` among its chunks) gets its own
+    // 2 KB of the stage area and nothing waits; otherwise two 2 KB buffers per
+    // warp alternate.
+    auto stage_store = [&](const uint32_t (&hw)[16], int row0, int col0, int chunk, bool big,
+                           int slot) {
       uint32_t buf;
       if (big) {
-        buf = sA + static_cast<uint32_t>((ew * Cfg::kChunksPerWarp + (chunk - chunk0)) *
-                                         Cfg::kEpiBufBytes);
+        buf = sA + static_cast<uint32_t>((ew * Cfg::kChunksPerWarp + slot) * Cfg::kEpiBufBytes);
       } else {
         buf = sEpi + static_cast<uint32_t>((ew * 2 + (chunk_count & 1)) * Cfg::kEpiBufBytes);
         ++chunk_count;
@@ -507,9 +547,15 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       }
     };
 
-    for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters) {
+    WorkIter<Cfg::kQuarters> it(p, cluster_id, num_clusters);
+    WorkUnit u;
+    while (ok && it.next(p, u)) {
       int mb, nb;
-      tile_coords(tile, p, mb, nb);
+      tile_coords(u.tile, p, mb, nb);
+      // This warp's chunks of the unit: the unit's n_unit / 32 chunks are
+      // split in two halves between the two warps of each lane quarter.
+      const int cpw = Cfg::kTailSplit ? u.w * (kQuarterCols / 64) : Cfg::kChunksPerWarp;
+      const int chunk0 = epi_chunk_begin(warp, cpw);
       if (!BM_WAIT(tfull_bar(acc), acc_phase, p.timeout_ns, abort_flag, kStatEpiWait, kStatEpiWaits)) {
         if (lane == 0) fail(kStatusEpilogueTimeout);
         break;
@@ -521,11 +567,11 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 2, ptx::globaltimer_ns());
 #endif
       const int row0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * 128 + quarter * 32;
-      const int col0 = nb * Cfg::kTileN;
+      const int col0 = nb * Cfg::kTileN + (Cfg::kTailSplit ? u.q0 * kQuarterCols : 0);
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
-      const bool last = tile + num_clusters >= p.num_tiles;
+      const bool last = it.done(p);
 
-      constexpr int kHalves = 2 * Cfg::kChunksPerWarp;
+      const int halves = 2 * cpw;
       const uint32_t t_w = t_acc + static_cast<uint32_t>(chunk0 * 32);
       // Hand the accumulator back to the MMA issuer once every TMEM read of
       // this warp has completed.
@@ -549,43 +595,56 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         ptx::tmem_ld_32x32b_x16(t_w, ra);
         ptx::tmem_wait_ld();
 #pragma unroll 1
-        for (int h = 0; h < kHalves; h += 2) {
+        for (int h = 0; h < halves; h += 2) {
           uint32_t hc[16];
           ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
 #pragma unroll
           for (int i = 0; i < 8; ++i) hc[i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
           ptx::tmem_wait_ld();
-          if (h + 2 < kHalves) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
+          if (h + 2 < halves) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
 #pragma unroll
           for (int i = 0; i < 8; ++i) hc[8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
-          stage_store(hc, row0, col0, chunk0 + h / 2, true);
-          if (h + 2 < kHalves) ptx::tmem_wait_ld();
+          stage_store(hc, row0, col0, chunk0 + h / 2, true, h / 2);
+          if (h + 2 < halves) ptx::tmem_wait_ld();
         }
         release_tmem();
       } else {
         // Read this warp's whole share of the accumulator into registers as
         // packed FP16 (load h+1 while packing h), hand TMEM back to the MMA
         // issuer, then store: the stores overlap the next tile's mainloop
-        // instead of holding TMEM.
-        uint32_t hw[Cfg::kChunksPerWarp][16];
-        uint32_t ra[16], rb[16];
-        ptx::tmem_ld_32x32b_x16(t_w, ra);
-        ptx::tmem_wait_ld();
-#pragma unroll
-        for (int h = 0; h < kHalves; h += 2) {
-          ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) hw[h / 2][i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
+        // instead of holding TMEM. One fully unrolled copy per unit width.
+        auto drain = [&](auto cpw_tag) {
+          constexpr int kCpw = decltype(cpw_tag)::value;
+          uint32_t hw[kCpw][16];
+          uint32_t ra[16], rb[16];
+          ptx::tmem_ld_32x32b_x16(t_w, ra);
           ptx::tmem_wait_ld();
-          if (h + 2 < kHalves) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) hw[h / 2][8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
-          if (h + 2 < kHalves) ptx::tmem_wait_ld();
+          for (int h = 0; h < 2 * kCpw; h += 2) {
+            ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hw[h / 2][i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
+            ptx::tmem_wait_ld();
+            if (h + 2 < 2 * kCpw) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hw[h / 2][8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
+            if (h + 2 < 2 * kCpw) ptx::tmem_wait_ld();
+          }
+          release_tmem();
+#pragma unroll
+          for (int cc = 0; cc < kCpw; ++cc) stage_store(hw[cc], row0, col0, chunk0 + cc, false, cc);
+        };
+        if constexpr (Cfg::kTailSplit) {
+          static_assert(Cfg::kChunksPerWarp == 8, "quarter runs of 1..4 quarters");
+          switch (cpw) {
+            case 2: drain(IntTag<2>{}); break;
+            case 4: drain(IntTag<4>{}); break;
+            case 6: drain(IntTag<6>{}); break;
+            default: drain(IntTag<8>{}); break;
+          }
+        } else {
+          drain(IntTag<Cfg::kChunksPerWarp>{});
         }
-        release_tmem();
-#pragma unroll
-        for (int cc = 0; cc < Cfg::kChunksPerWarp; ++cc)
-          stage_store(hw[cc], row0, col0, chunk0 + cc, false);
       }
 #if defined(BM_KERNEL_STATS)
       st[kStatEpiBusy] += static_cast<unsigned long long>(clock64() - t_epi);
