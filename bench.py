@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--size", type=int, default=SIZE, help="M (per rank) = N = K")
     ap.add_argument("--variant", type=int, default=0)
+    ap.add_argument("--split", choices=["none", "auto"], default="auto",
+                    help="schedule of leftover tiles (bm_gemm_set_split)")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -267,9 +269,11 @@ def main():
             a, b, c = bm.alloc_operands(m, n, k, layout, device=dev, mode=4, seed=s,
                                         row0=rank * m, total_m=world * m)
             g = bm.Gemm.from_tensors(a, b, c, layout, variant=args.variant)
+            g.set_split(bm.SPLIT_NONE if args.split == "none" else bm.SPLIT_AUTO)
             entry[layout] = (a, b, c, g)
         sets.append(entry)
     info = {l: sets[0][l][3].info() for l in ("NT", "TN")}
+    sched = sets[0]["NT"][3].schedule()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
 
@@ -476,6 +480,7 @@ def main():
                       "> 3x L2 between reuses",
                 "kernels": {l: info[l]["name"] for l in info},
                 "grid": {l: info[l]["grid"][0] for l in info},
+                "schedule": dict(sched, split=args.split),
             },
             "roofline": roofline, "cpu_baseline": cpu_baseline, "e2e": e2e,
             "gpu_launches": LAUNCHES_PER_STEP * args.steps, "clocks": clocks.summary(),
