@@ -78,9 +78,9 @@ class GemmDesc(ctypes.Structure):
 class ScheduleInfo(ctypes.Structure):
     _fields_ = [
         ("whole_tiles", ctypes.c_int), ("split_tiles", ctypes.c_int),
-        ("split_quarters", ctypes.c_int), ("split_clusters", ctypes.c_int),
+        ("split_parts", ctypes.c_int), ("split_clusters", ctypes.c_int),
         ("grid_clusters", ctypes.c_int), ("resident_clusters", ctypes.c_int),
-        ("quarter_cols", ctypes.c_int),
+        ("split_cols", ctypes.c_int),
     ]
 
 

@@ -76,7 +76,7 @@ struct bm_gemm_handle {
   uint32_t* d_status;
   LaunchFn launch;
   int max_clusters;  // resident clusters of this variant on this device
-  int quarters;      // column quarters per tile the variant can split into (1: none)
+  int parts;         // column parts per tile the variant can split into (1: none)
   int split_mode;    // enum bm_split_mode
 };
 
@@ -210,20 +210,20 @@ int resolve(const bm_gemm_desc* d, Resolved* r) {
   return BM_OK;
 }
 
-// Column quarters a variant's leftover tiles can be split into (1 = whole
+// Column parts a variant's leftover tiles can be split into (1 = whole
 // tiles only): the 256x512 pair tile (GemmConfig::kTailSplit).
-int split_quarters(int variant) {
+int split_parts(int variant) {
   const VariantInfo& vi = kVariants[variant];
-  return (vi.cta_group == 2 && vi.mma_n == 256 && vi.num_n == 2) ? (vi.mma_n * vi.num_n) / bm::kQuarterCols
+  return (vi.cta_group == 2 && vi.mma_n == 256 && vi.num_n == 2) ? (vi.mma_n * vi.num_n) / bm::kSplitCols
                                                                    : 1;
 }
 
 void apply_plan(bm_gemm_handle* h) {
   GemmParams& p = h->params;
-  const bm::Plan pl = bm::plan_schedule(p.num_tiles, h->quarters, h->max_clusters,
+  const bm::Plan pl = bm::plan_schedule(p.num_tiles, h->parts, h->max_clusters,
                                         h->split_mode == BM_SPLIT_AUTO ? 1 : 0);
   p.dp_tiles = pl.dp_tiles;
-  p.tail_quarters = pl.tail_quarters;
+  p.tail_parts = pl.tail_parts;
   p.tail_clusters = pl.tail_clusters;
   h->grid = pl.grid_clusters * h->cta_group;
 }
@@ -248,8 +248,8 @@ int pick_variant(const bm_gemm_desc* d) {
     const long long tm = 128LL * vi.cta_group, tn = static_cast<long long>(vi.mma_n) * vi.num_n;
     const long long tiles = ((d->m + tm - 1) / tm) * ((d->n + tn - 1) / tn);
     const int slots = sms / vi.cta_group;
-    // waves as scheduled (leftover tiles split into quarters where possible)
-    const bm::Plan pl = bm::plan_schedule(static_cast<int>(tiles), split_quarters(c.id), slots, 1);
+    // waves as scheduled (leftover tiles split into halves where that pays)
+    const bm::Plan pl = bm::plan_schedule(static_cast<int>(tiles), split_parts(c.id), slots, 1);
     const double busy = static_cast<double>(tiles) / (static_cast<double>(slots) * pl.est);
     const double score = c.eff * busy;
     if (score > best_score + 1e-9) {
@@ -384,7 +384,7 @@ int bm_gemm_prepare(const bm_gemm_desc* d, bm_gemm_handle** out) {
   p.debug = 0;
   p.stats = nullptr;
   h->max_clusters = max_clusters;
-  h->quarters = split_quarters(v);
+  h->parts = split_parts(v);
   h->split_mode = BM_SPLIT_AUTO;
   apply_plan(h);
 
@@ -459,11 +459,11 @@ int bm_gemm_query_schedule(const bm_gemm_handle* h, bm_schedule_info* info) {
   const GemmParams& p = h->params;
   info->whole_tiles = p.dp_tiles;
   info->split_tiles = p.num_tiles - p.dp_tiles;
-  info->split_quarters = p.tail_quarters;
+  info->split_parts = p.tail_parts;
   info->split_clusters = p.tail_clusters;
   info->grid_clusters = h->grid / h->cta_group;
   info->resident_clusters = h->max_clusters;
-  info->quarter_cols = h->quarters > 1 ? bm::kQuarterCols : 0;
+  info->split_cols = h->parts > 1 ? bm::kSplitCols : 0;
   return BM_OK;
 }
 
@@ -640,7 +640,7 @@ extern "C" int bm_gemm_run_noalloc(const bm_gemm_desc* d, void* stream, uint32_t
   p.stats = nullptr;
   p.status = nd.scratch;
   p.dp_tiles = p.num_tiles;  // whole tiles, one wave after another
-  p.tail_quarters = 0;
+  p.tail_parts = 0;
   p.tail_clusters = 0;
   const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
   h.grid = clusters * h.cta_group;

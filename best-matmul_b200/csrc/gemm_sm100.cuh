@@ -64,11 +64,11 @@ struct GemmParams {
   uint32_t debug;        // kDebug* flags; 0 in production
   unsigned long long* stats;  // per-CTA cycle counters; only read in BM_KERNEL_STATS builds
   // Schedule (schedule.cuh): tiles [0, dp_tiles) whole, cluster c taking c,
-  // c + clusters, ...; then the column quarters of tiles [dp_tiles,
-  // num_tiles) split over clusters [0, tail_clusters) (tail_quarters = 0:
+  // c + clusters, ...; then the column halves of tiles [dp_tiles,
+  // num_tiles) split over clusters [0, tail_clusters) (tail_parts = 0:
   // nothing split).
   int dp_tiles;
-  int tail_quarters;
+  int tail_parts;
   int tail_clusters;
 };
 
@@ -144,11 +144,11 @@ struct GemmConfig {
   static constexpr int kOffAbort = kOffTmemSlot + 4;
   static constexpr int kSmemBytes = kOffAbort + 4 + 1024;  // + alignment slack
   static constexpr uint32_t kIdesc = make_idesc_f16_f32(kMmaM, kBN, kMnMajor);
-  // Column quarters per tile, and whether leftover tiles may be computed in
-  // quarter runs (the 256x512 pair tile: runs of 128..512 columns map onto
-  // one or two MMAs of N = 128 or 256, B rows per CTA stay multiples of 64).
-  static constexpr int kQuarters = kTileN / kQuarterCols;
+  // Column parts per tile, and whether leftover tiles may be computed in
+  // parts (the 256x512 pair tile: a 256-column half is one N = 256 MMA per
+  // K step instead of two).
   static constexpr bool kTailSplit = (kCtaGroup == 2 && kNumN == 2 && kBN == 256);
+  static constexpr int kParts = kTailSplit ? kTileN / kSplitCols : 1;
 
   static_assert(kBN == 128 || kBN == 256, "kBN must be 128 or 256");
   static_assert(kNumN == 1 || kNumN == 2, "kNumN must be 1 or 2");
@@ -289,7 +289,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      WorkIter<Cfg::kQuarters> it(p, cluster_id, num_clusters);
+      WorkIter<Cfg::kParts> it(p, cluster_id, num_clusters);
       WorkUnit u;
       while (ok && it.next(p, u)) {
         int mb, nb;
@@ -297,8 +297,8 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         // Columns of this unit: n_unit from nbase; MMA j covers
         // [nbase + j*kBN, + nj), nj = min(n_unit - j*kBN, kBN) (<= 0: no MMA j),
         // and this CTA holds B rows [rank * nj / kCtaGroup, + nj / kCtaGroup).
-        const int n_unit = Cfg::kTailSplit ? u.w * kQuarterCols : Cfg::kTileN;
-        const int nbase = nb * Cfg::kTileN + (Cfg::kTailSplit ? u.q0 * kQuarterCols : 0);
+        const int n_unit = Cfg::kTailSplit ? u.w * kSplitCols : Cfg::kTileN;
+        const int nbase = nb * Cfg::kTileN + (Cfg::kTailSplit ? u.q0 * kSplitCols : 0);
         const int m0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * Cfg::kRowsA;
         // Bytes this CTA lands per stage. K-major B loads whole boxes of
         // kRowsBPerMma rows even when a narrower MMA uses only the first half.
@@ -386,11 +386,11 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       uint32_t acc_phase = 0;
       bool ok = true;
       const uint32_t peer = 1u;
-      WorkIter<Cfg::kQuarters> it(p, cluster_id, num_clusters);
+      WorkIter<Cfg::kParts> it(p, cluster_id, num_clusters);
       WorkUnit u;
       while (ok && it.next(p, u)) {
         // N of MMA j for this unit (whole tiles: kBN each, compile-time).
-        const int n_unit = Cfg::kTailSplit ? u.w * kQuarterCols : Cfg::kTileN;
+        const int n_unit = Cfg::kTailSplit ? u.w * kSplitCols : Cfg::kTileN;
         const int n0 = Cfg::kTailSplit ? min(n_unit, kBN) : kBN;
         const int n1 = Cfg::kTailSplit ? n_unit - kBN : kBN;
         const uint32_t idesc0 = Cfg::kTailSplit ? make_idesc_f16_f32(Cfg::kMmaM, n0, kMnMajor) : Cfg::kIdesc;
@@ -547,14 +547,14 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       }
     };
 
-    WorkIter<Cfg::kQuarters> it(p, cluster_id, num_clusters);
+    WorkIter<Cfg::kParts> it(p, cluster_id, num_clusters);
     WorkUnit u;
     while (ok && it.next(p, u)) {
       int mb, nb;
       tile_coords(u.tile, p, mb, nb);
       // This warp's chunks of the unit: the unit's n_unit / 32 chunks are
       // split in two halves between the two warps of each lane quarter.
-      const int cpw = Cfg::kTailSplit ? u.w * (kQuarterCols / 64) : Cfg::kChunksPerWarp;
+      const int cpw = Cfg::kTailSplit ? u.w * (kSplitCols / 64) : Cfg::kChunksPerWarp;
       const int chunk0 = epi_chunk_begin(warp, cpw);
       if (!BM_WAIT(tfull_bar(acc), acc_phase, p.timeout_ns, abort_flag, kStatEpiWait, kStatEpiWaits)) {
         if (lane == 0) fail(kStatusEpilogueTimeout);
@@ -567,7 +567,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 2, ptx::globaltimer_ns());
 #endif
       const int row0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * 128 + quarter * 32;
-      const int col0 = nb * Cfg::kTileN + (Cfg::kTailSplit ? u.q0 * kQuarterCols : 0);
+      const int col0 = nb * Cfg::kTileN + (Cfg::kTailSplit ? u.q0 * kSplitCols : 0);
       const uint32_t t_acc = tmem_base + lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
       const bool last = it.done(p);
 
@@ -635,13 +635,9 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           for (int cc = 0; cc < kCpw; ++cc) stage_store(hw[cc], row0, col0, chunk0 + cc, false, cc);
         };
         if constexpr (Cfg::kTailSplit) {
-          static_assert(Cfg::kChunksPerWarp == 8, "quarter runs of 1..4 quarters");
-          switch (cpw) {
-            case 2: drain(IntTag<2>{}); break;
-            case 4: drain(IntTag<4>{}); break;
-            case 6: drain(IntTag<6>{}); break;
-            default: drain(IntTag<8>{}); break;
-          }
+          static_assert(Cfg::kChunksPerWarp == 8 && kSplitCols == 256, "units of one or two halves");
+          if (cpw == 4) drain(IntTag<4>{});
+          else drain(IntTag<8>{});
         } else {
           drain(IntTag<Cfg::kChunksPerWarp>{});
         }

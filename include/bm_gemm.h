@@ -134,11 +134,11 @@ void bm_gemm_destroy(bm_gemm_handle* handle);
  * grid is one CTA per output tile (kernels/detail/tma_wgmma_adapter.cuh:96-113)
  * and so leaves its last wave partly idle whenever the tile count is not a
  * multiple of the CTAs resident at once.
- *   BM_SPLIT_AUTO (default) whole tiles fill complete waves; the tiles left
- *                 for a partly idle last wave are cut into 128-column
- *                 quarters and every cluster computes a contiguous run of
- *                 them (full K range, narrower MMAs), when that shortens the
- *                 last wave. Only the 2-CTA 256x512 variant splits.
+ *   BM_SPLIT_AUTO (default) whole tiles fill complete waves; when the tiles
+ *                 left for the last wave are at most half the resident
+ *                 clusters, they are cut into 256-column halves (full K
+ *                 range, one N = 256 MMA per K step) that twice as many
+ *                 clusters share. Only the 2-CTA 256x512 variant splits.
  *   BM_SPLIT_NONE whole tiles only.
  * Each output element is still computed by one MMA chain over all of K in the
  * same order, so both modes give the same bits; nothing is allocated and no
@@ -147,12 +147,12 @@ enum bm_split_mode { BM_SPLIT_NONE = 0, BM_SPLIT_AUTO = 1 };
 
 typedef struct bm_schedule_info {
   int whole_tiles;       /* tiles computed whole, in full waves */
-  int split_tiles;       /* tiles computed as quarter runs */
-  int split_quarters;    /* quarters of those tiles */
-  int split_clusters;    /* clusters sharing the quarters */
+  int split_tiles;       /* tiles computed in column parts */
+  int split_parts;       /* parts of those tiles */
+  int split_clusters;    /* clusters sharing the parts */
   int grid_clusters;     /* clusters launched */
   int resident_clusters; /* clusters that fit on the device at once */
-  int quarter_cols;      /* columns per quarter (0: variant never splits) */
+  int split_cols;        /* columns per part (0: variant never splits) */
 } bm_schedule_info;
 
 /* Re-plan a prepared handle's schedule (mode: enum bm_split_mode). Host-side

@@ -2,16 +2,16 @@
 // runs the kernel's own planner and work iterator for every cluster of a
 // grid and verifies what the kernel relies on.
 //
-//   schedule_check                    sweep of tile counts, quarters, clusters
+//   schedule_check                    sweep of tile counts, parts, clusters
 //   schedule_check T Q C SPLIT        one case, units printed
 //
 // Per case:
-//   1. every column quarter of every tile is computed by exactly one unit;
+//   1. every column part of every tile is computed by exactly one unit;
 //   2. units stay inside their tile (0 <= q0, q0 + w <= Q, w >= 1);
 //   3. whole tiles come first and fill complete waves (dp_tiles % C == 0
 //      whenever anything is split), and a cluster's units are whole tiles
-//      first, then at most two runs of quarters;
-//   4. no cluster computes more quarters of split tiles than the plan's run;
+//      first, then at most two runs of parts;
+//   4. no cluster computes more parts of split tiles than the plan's run;
 //   5. the grid covers every cluster that has work, within the resident ones;
 //   6. done() is true exactly when next() has nothing left.
 // Exit status 0 when every case holds.
@@ -24,28 +24,28 @@
 namespace {
 
 struct Params {
-  int dp_tiles, tail_quarters, tail_clusters;
+  int dp_tiles, tail_parts, tail_clusters;
 };
 
 int g_fail = 0;
 
 void fail(const char* what, int t, int q, int c, int split) {
-  if (g_fail < 20) std::printf("FAIL %s (tiles=%d quarters=%d clusters=%d split=%d)\n", what, t, q, c, split);
+  if (g_fail < 20) std::printf("FAIL %s (tiles=%d parts=%d clusters=%d split=%d)\n", what, t, q, c, split);
   ++g_fail;
 }
 
 template <int Q>
 bool check_case(int tiles, int clusters, int split, bool print) {
   const bm::Plan pl = bm::plan_schedule(tiles, Q, clusters, split);
-  const Params p{pl.dp_tiles, pl.tail_quarters, pl.tail_clusters};
+  const Params p{pl.dp_tiles, pl.tail_parts, pl.tail_clusters};
   const int before = g_fail;
-  const bool splits = pl.tail_quarters > 0;
+  const bool splits = pl.tail_parts > 0;
   if (splits && pl.dp_tiles % clusters != 0) fail("whole tiles not full waves", tiles, Q, clusters, split);
-  if (splits && pl.tail_quarters != (tiles - pl.dp_tiles) * Q) fail("tail quarter count", tiles, Q, clusters, split);
+  if (splits && pl.tail_parts != (tiles - pl.dp_tiles) * Q) fail("tail part count", tiles, Q, clusters, split);
   if (pl.grid_clusters > clusters || pl.tail_clusters > pl.grid_clusters)
     fail("grid", tiles, Q, clusters, split);
   if (!split && splits) fail("split while disabled", tiles, Q, clusters, split);
-  const int run = splits ? (pl.tail_quarters + clusters - 1) / clusters : Q;
+  const int run = splits ? (pl.tail_parts + clusters - 1) / clusters : Q;
   std::vector<int> cover(static_cast<size_t>(tiles) * Q, 0);
   for (int c = 0; c < pl.grid_clusters; ++c) {
     bm::WorkIter<Q> it(p, c, pl.grid_clusters);
@@ -57,7 +57,7 @@ bool check_case(int tiles, int clusters, int split, bool print) {
       const bool got = it.next(p, u);
       if (done == got) fail("done() disagrees with next()", tiles, Q, clusters, split);
       if (!got) break;
-      if (print) std::printf("cluster %d: tile %d quarters [%d,%d)\n", c, u.tile, u.q0, u.q0 + u.w);
+      if (print) std::printf("cluster %d: tile %d parts [%d,%d)\n", c, u.tile, u.q0, u.q0 + u.w);
       if (u.tile < 0 || u.tile >= tiles || u.w < 1 || u.q0 < 0 || u.q0 + u.w > Q) {
         fail("unit out of range", tiles, Q, clusters, split);
         continue;
@@ -77,7 +77,7 @@ bool check_case(int tiles, int clusters, int split, bool print) {
   }
   for (size_t i = 0; i < cover.size(); ++i)
     if (cover[i] != 1) {
-      fail("quarter not covered exactly once", tiles, Q, clusters, split);
+      fail("part not covered exactly once", tiles, Q, clusters, split);
       break;
     }
   return g_fail == before;
@@ -105,11 +105,11 @@ int main(int argc, char** argv) {
       case 1: ok = check_case<1>(t, c, s, true); break;
       case 2: ok = check_case<2>(t, c, s, true); break;
       case 4: ok = check_case<4>(t, c, s, true); break;
-      default: std::printf("quarters must be 1, 2 or 4\n"); return 2;
+      default: std::printf("parts must be 1, 2 or 4\n"); return 2;
     }
     const bm::Plan pl = bm::plan_schedule(t, q, c, s);
-    std::printf("plan dp_tiles=%d tail_quarters=%d tail_clusters=%d grid=%d est=%.4f\n", pl.dp_tiles,
-                pl.tail_quarters, pl.tail_clusters, pl.grid_clusters, pl.est);
+    std::printf("plan dp_tiles=%d tail_parts=%d tail_clusters=%d grid=%d est=%.4f\n", pl.dp_tiles,
+                pl.tail_parts, pl.tail_clusters, pl.grid_clusters, pl.est);
     return ok ? 0 : 1;
   }
   const long long n = sweep<1>() + sweep<2>() + sweep<4>();
