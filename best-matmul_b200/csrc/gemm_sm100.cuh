@@ -148,6 +148,11 @@ struct GemmConfig {
   // parts (the 256x512 pair tile: a 256-column half is one N = 256 MMA per
   // K step instead of two).
   static constexpr bool kTailSplit = (kCtaGroup == 2 && kNumN == 2 && kBN == 256);
+  // One accumulator of 512 columns whose halves the epilogue releases one
+  // after the other: tempty_bar(0) frees columns [0, 256), tempty_bar(1)
+  // columns [256, 512) (kAccStages == 1 leaves the second barrier free).
+  static constexpr bool kHalfRelease = kTailSplit;
+  static_assert(!kHalfRelease || (kAccStages == 1 && kTileN == 512), "half release layout");
   static constexpr int kParts = kTailSplit ? kTileN / kSplitCols : 1;
 
   static_assert(kBN == 128 || kBN == 256, "kBN must be 128 or 256");
@@ -163,8 +168,11 @@ struct GemmConfig {
 };
 
 // Epilogue ownership (shared with the host-side mapping check): epilogue warp
-// `warp` (2..9) reads TMEM lane quarter warp % 4 and, of each accumulator's
-// kChunks 32-column chunks, the half starting at epi_chunk_begin(). In chunk
+// `warp` (2..9) reads TMEM lane quarter warp % 4; the two warps of a quarter
+// share a unit's 32-column chunks, cpw each, the warp's cc-th chunk being
+// epi_chunk(warp, cc, cpw, half_order). With half_order (the 256x512 pair
+// tile) both warps first take chunks of columns [0, 256) and then of
+// [256, 512), so that the first TMEM half can be released early. In chunk
 // `chunk`, step i (0..15), lane `lane` stores one 32-bit word: two consecutive
 // rows of one column of the CTA's 128-row tile.
 struct EpiCoord {
@@ -172,8 +180,9 @@ struct EpiCoord {
   int col;  // column within the tile
 };
 __host__ __device__ constexpr int epi_quarter(int warp) { return warp & 3; }
-__host__ __device__ constexpr int epi_chunk_begin(int warp, int chunks_per_warp) {
-  return ((warp - 2) / 4) * chunks_per_warp;
+__host__ __device__ constexpr bool epi_half_order(int tile_n) { return tile_n == 512; }
+__host__ __device__ constexpr int epi_chunk(int warp, int cc, int cpw, bool half_order) {
+  return half_order ? (cc / 4) * 8 + ((warp - 2) / 4) * 4 + cc % 4 : ((warp - 2) / 4) * cpw + cc;
 }
 __host__ __device__ constexpr EpiCoord epi_word_coord(int warp, int lane, int chunk, int i) {
   return EpiCoord{epi_quarter(warp) * 32 + (lane & ~1), chunk * 32 + 2 * i + (lane & 1)};
@@ -407,15 +416,10 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         unit_wait0 = st[kStatMmaFullWait];
 #endif
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!BM_WAIT(full_bar(stage), phase, p.timeout_ns, abort_flag, kStatMmaFullWait, kStatMmaFullWaits)) {
-            fail(kStatusMmaTimeout);
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
-          const uint32_t a_base = sA + stage * Cfg::kBytesA;
-          const uint32_t b_base = sB + stage * Cfg::kBytesB;
+        // MMAs j in [jlo, jhi) of k-block kb from stage stg.
+        auto issue = [&](int stg, int kb, int jlo, int jhi) {
+          const uint32_t a_base = sA + stg * Cfg::kBytesA;
+          const uint32_t b_base = sB + stg * Cfg::kBytesB;
 #pragma unroll
           for (int ks = 0; ks < Cfg::kBK / 16; ++ks) {
             // MN-major: 64 MN-elements per 128-byte row, one row per k; 8-row
@@ -428,7 +432,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint64_t a_desc = ptx::smem_desc_sw128(a_base + koff, lbo, 1024);
 #pragma unroll
             for (int j = 0; j < kNumN; ++j) {
-              if (j >= n_mma) break;
+              if (j < jlo || j >= jhi || j >= n_mma) continue;
               const uint64_t b_desc =
                   ptx::smem_desc_sw128(b_base + j * Cfg::kBytesBPerMma + koff, lbo, 1024);
 #if defined(BM_KERNEL_STATS)
@@ -438,12 +442,58 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                       j == 0 ? idesc0 : idesc1, (kb > 0 || ks > 0) ? 1u : 0u);
             }
           }
-          // Free this stage in every CTA that loaded into it.
-          ptx::mma_commit<kCtaGroup>(empty_bar(stage));
-          if constexpr (kCtaGroup == 2) ptx::mma_commit<kCtaGroup>(ptx::mapa(empty_bar(stage), peer));
+        };
+        // Free a stage in every CTA that loaded into it.
+        auto release_stage = [&](int stg) {
+          ptx::mma_commit<kCtaGroup>(empty_bar(stg));
+          if constexpr (kCtaGroup == 2) ptx::mma_commit<kCtaGroup>(ptx::mapa(empty_bar(stg), peer));
 #if defined(BM_KERNEL_STATS)
           st[kStatKBlocks] += 1;
 #endif
+        };
+        int kb = 0;
+        if constexpr (Cfg::kHalfRelease) {
+          // The epilogue hands back TMEM columns [0, 256) first: run MMA 0 of
+          // the first kStages k-blocks (already loaded while the previous
+          // tile drained) into them, then, once [256, 512) is free too, MMA 1
+          // of the same k-blocks, releasing each stage after both.
+          const int pre = p.k_blocks < kStages ? p.k_blocks : kStages;
+          const int stage0 = stage;
+          for (; kb < pre; ++kb) {
+            if (!BM_WAIT(full_bar(stage), phase, p.timeout_ns, abort_flag, kStatMmaFullWait, kStatMmaFullWaits)) {
+              fail(kStatusMmaTimeout);
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            issue(stage, kb, 0, 1);
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          if (!BM_WAIT(tempty_bar(1), acc_phase ^ 1u, p.timeout_ns, abort_flag, kStatMmaTmemWait, kStatMmaTmemWaits)) {
+            fail(kStatusMmaTimeout);
+            break;
+          }
+          ptx::tc_fence_after();
+          int s2 = stage0;
+          for (int k2 = 0; k2 < pre; ++k2) {
+            issue(s2, k2, 1, kNumN);
+            release_stage(s2);
+            if (++s2 == kStages) s2 = 0;
+          }
+        }
+        for (; kb < p.k_blocks; ++kb) {
+          if (!BM_WAIT(full_bar(stage), phase, p.timeout_ns, abort_flag, kStatMmaFullWait, kStatMmaFullWaits)) {
+            fail(kStatusMmaTimeout);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          issue(stage, kb, 0, kNumN);
+          release_stage(stage);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -555,7 +605,6 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       // This warp's chunks of the unit: the unit's n_unit / 32 chunks are
       // split in two halves between the two warps of each lane quarter.
       const int cpw = Cfg::kTailSplit ? u.w * (kSplitCols / 64) : Cfg::kChunksPerWarp;
-      const int chunk0 = epi_chunk_begin(warp, cpw);
       if (!BM_WAIT(tfull_bar(acc), acc_phase, p.timeout_ns, abort_flag, kStatEpiWait, kStatEpiWaits)) {
         if (lane == 0) fail(kStatusEpilogueTimeout);
         break;
@@ -572,17 +621,23 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const bool last = it.done(p);
 
       const int halves = 2 * cpw;
-      const uint32_t t_w = t_acc + static_cast<uint32_t>(chunk0 * 32);
-      // Hand the accumulator back to the MMA issuer once every TMEM read of
-      // this warp has completed.
-      auto release_tmem = [&]() {
+      constexpr bool kHalfOrder = epi_half_order(Cfg::kTileN);
+      auto chunk_of = [&](int cc) { return epi_chunk(warp, cc, cpw, kHalfOrder); };
+      // Hand TMEM back to the MMA issuer once this warp's reads of it have
+      // completed: the whole accumulator (barrier acc), or with kHalfRelease
+      // columns [0, 256) (h = 0) and [256, 512) (h = 1) separately.
+      auto arrive_tempty = [&](int h) {
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          const uint32_t tb = acc ? tempty_leader1 : tempty_leader0;
+          const uint32_t tb = h ? tempty_leader1 : tempty_leader0;
           if constexpr (kCtaGroup == 2) ptx::mbar_arrive_cluster(tb);
           else ptx::mbar_arrive(tb);
         }
+      };
+      auto release_tmem = [&]() {
+        if constexpr (Cfg::kHalfRelease) arrive_tempty(1);
+        else arrive_tempty(acc);
 #if defined(BM_KERNEL_STATS)
         if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 3, ptx::globaltimer_ns());
 #endif
@@ -592,21 +647,24 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         // packed, so TMEM reads and stores overlap (16-column TMEM loads,
         // double-buffered).
         uint32_t ra[16], rb[16];
-        ptx::tmem_ld_32x32b_x16(t_w, ra);
+        ptx::tmem_ld_32x32b_x16(t_acc + static_cast<uint32_t>(chunk_of(0) * 32), ra);
         ptx::tmem_wait_ld();
 #pragma unroll 1
         for (int h = 0; h < halves; h += 2) {
           uint32_t hc[16];
-          ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
+          const int ch = chunk_of(h / 2);
+          ptx::tmem_ld_32x32b_x16(t_acc + static_cast<uint32_t>(ch * 32 + 16), rb);
 #pragma unroll
           for (int i = 0; i < 8; ++i) hc[i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
           ptx::tmem_wait_ld();
-          if (h + 2 < halves) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
+          if (h + 2 < halves)
+            ptx::tmem_ld_32x32b_x16(t_acc + static_cast<uint32_t>(chunk_of(h / 2 + 1) * 32), ra);
 #pragma unroll
           for (int i = 0; i < 8; ++i) hc[8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
-          stage_store(hc, row0, col0, chunk0 + h / 2, true, h / 2);
+          stage_store(hc, row0, col0, ch, true, h / 2);
           if (h + 2 < halves) ptx::tmem_wait_ld();
         }
+        if constexpr (Cfg::kHalfRelease) arrive_tempty(0);
         release_tmem();
       } else {
         // Read this warp's whole share of the accumulator into registers as
@@ -617,22 +675,28 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           constexpr int kCpw = decltype(cpw_tag)::value;
           uint32_t hw[kCpw][16];
           uint32_t ra[16], rb[16];
-          ptx::tmem_ld_32x32b_x16(t_w, ra);
+          ptx::tmem_ld_32x32b_x16(t_acc + static_cast<uint32_t>(chunk_of(0) * 32), ra);
           ptx::tmem_wait_ld();
 #pragma unroll
           for (int h = 0; h < 2 * kCpw; h += 2) {
-            ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 1) * 16), rb);
+            ptx::tmem_ld_32x32b_x16(t_acc + static_cast<uint32_t>(chunk_of(h / 2) * 32 + 16), rb);
 #pragma unroll
             for (int i = 0; i < 8; ++i) hw[h / 2][i] = pack_pair(ra[2 * i], ra[2 * i + 1]);
             ptx::tmem_wait_ld();
-            if (h + 2 < 2 * kCpw) ptx::tmem_ld_32x32b_x16(t_w + static_cast<uint32_t>((h + 2) * 16), ra);
+            // With the half order, chunks 0..3 of this warp are its share of
+            // TMEM columns [0, 256): hand those back before reading the rest.
+            if constexpr (Cfg::kHalfRelease) {
+              if (h / 2 == 3) arrive_tempty(0);
+            }
+            if (h + 2 < 2 * kCpw)
+              ptx::tmem_ld_32x32b_x16(t_acc + static_cast<uint32_t>(chunk_of(h / 2 + 1) * 32), ra);
 #pragma unroll
             for (int i = 0; i < 8; ++i) hw[h / 2][8 + i] = pack_pair(rb[2 * i], rb[2 * i + 1]);
             if (h + 2 < 2 * kCpw) ptx::tmem_wait_ld();
           }
           release_tmem();
 #pragma unroll
-          for (int cc = 0; cc < kCpw; ++cc) stage_store(hw[cc], row0, col0, chunk0 + cc, false, cc);
+          for (int cc = 0; cc < kCpw; ++cc) stage_store(hw[cc], row0, col0, chunk_of(cc), false, cc);
         };
         if constexpr (Cfg::kTailSplit) {
           static_assert(Cfg::kChunksPerWarp == 8 && kSplitCols == 256, "units of one or two halves");

@@ -38,8 +38,9 @@ bool check_output_mapping(int tile_n) {
   std::vector<int> owners(static_cast<std::size_t>(128) * tile_n, 0);
   for (int warp = 2; warp < 2 + bm::kEpiWarps; ++warp)
     for (int lane = 0; lane < 32; ++lane)
-      for (int c = bm::epi_chunk_begin(warp, per_warp); c < bm::epi_chunk_begin(warp, per_warp) + per_warp; ++c)
+      for (int cc = 0; cc < per_warp; ++cc)
         for (int i = 0; i < 16; ++i) {
+          const int c = bm::epi_chunk(warp, cc, per_warp, bm::epi_half_order(tile_n));
           // each lane stores one word = rows (row, row + 1) of one column
           const bm::EpiCoord e = bm::epi_word_coord(warp, lane, c, i);
           for (int r = 0; r < 2; ++r) {
