@@ -298,34 +298,57 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      WorkIter<Cfg::kParts> it(p, cluster_id, num_clusters);
-      WorkUnit u;
-      while (ok && it.next(p, u)) {
+      // Every TMA box of k-block kb of unit w for this CTA:
+      // f(is_b, byte offset in the stage's A or B part, tensor map, x, y).
+      // Columns of the unit: n_unit from nbase; MMA j covers
+      // [nbase + j*kBN, + nj), nj = min(n_unit - j*kBN, kBN) (<= 0: no MMA j),
+      // and this CTA holds B rows [rank * nj / kCtaGroup, + nj / kCtaGroup).
+      // MN-major (NT) tiles are 64-wide boxes 8 KB apart; K-major (TN) tiles
+      // are one box per operand and MMA (whole boxes of kRowsBPerMma rows).
+      auto unit_boxes = [&](const WorkUnit& w, int kb, auto&& f) {
         int mb, nb;
-        tile_coords(u.tile, p, mb, nb);
-        // Columns of this unit: n_unit from nbase; MMA j covers
-        // [nbase + j*kBN, + nj), nj = min(n_unit - j*kBN, kBN) (<= 0: no MMA j),
-        // and this CTA holds B rows [rank * nj / kCtaGroup, + nj / kCtaGroup).
-        const int n_unit = Cfg::kTailSplit ? u.w * kSplitCols : Cfg::kTileN;
-        const int nbase = nb * Cfg::kTileN + (Cfg::kTailSplit ? u.q0 * kSplitCols : 0);
+        tile_coords(w.tile, p, mb, nb);
+        const int n_unit = Cfg::kTailSplit ? w.w * kSplitCols : Cfg::kTileN;
+        const int nbase = nb * Cfg::kTileN + (Cfg::kTailSplit ? w.q0 * kSplitCols : 0);
         const int m0 = mb * Cfg::kTileM + static_cast<int>(cta_rank) * Cfg::kRowsA;
-        // Bytes this CTA lands per stage. K-major B loads whole boxes of
-        // kRowsBPerMma rows even when a narrower MMA uses only the first half.
-        uint32_t stage_bytes = Cfg::kBytesA;
+        const int k0 = kb * Cfg::kBK;
+        if constexpr (kMnMajor) {
+          f(false, 0u, &tmap_a, m0, k0);
+          f(false, 8192u, &tmap_a, m0 + 64, k0);
+        } else {
+          f(false, 0u, &tmap_a, k0, m0);
+        }
 #pragma unroll
         for (int j = 0; j < kNumN; ++j) {
           const int nj = min(n_unit - j * kBN, kBN);
-          if (nj > 0)
-            stage_bytes += kMnMajor ? static_cast<uint32_t>(nj / kCtaGroup) * (Cfg::kBK * 2)
-                                    : static_cast<uint32_t>(Cfg::kBytesBPerMma);
+          if (nj <= 0) break;
+          const int rows = nj / kCtaGroup;
+          const int r0 = nbase + j * kBN + static_cast<int>(cta_rank) * rows;
+          const uint32_t off = static_cast<uint32_t>(j * Cfg::kBytesBPerMma);
+          if constexpr (kMnMajor) {
+#pragma unroll
+            for (int q = 0; q < Cfg::kRowsBPerMma / 64; ++q)
+              if (64 * q < rows) f(true, off + 8192u * q, &tmap_b, r0 + 64 * q, k0);
+          } else {
+            f(true, off, &tmap_b, k0, r0);
+          }
         }
+      };
+      WorkIter<Cfg::kParts> it(p, cluster_id, num_clusters);
+      WorkUnit u;
+      while (ok && it.next(p, u)) {
+        // Bytes this CTA lands per stage for this unit.
+        uint32_t stage_bytes = 0;
+        unit_boxes(u, 0, [&](bool is_b, uint32_t, const CUtensorMap*, int, int) {
+          stage_bytes += is_b ? (kMnMajor ? 8192u : static_cast<uint32_t>(Cfg::kBytesBPerMma))
+                              : (kMnMajor ? 8192u : static_cast<uint32_t>(Cfg::kBytesA));
+        });
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!BM_WAIT(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, kStatProdWait, kStatProdWaits)) {
             fail(kStatusProducerTimeout);
             ok = false;
             break;
           }
-          const int k0 = kb * Cfg::kBK;
           const uint32_t a_dst = sA + stage * Cfg::kBytesA;
           const uint32_t b_dst = sB + stage * Cfg::kBytesB;
           // Completion bytes go to this CTA's barrier (1 CTA) or the pair
@@ -338,37 +361,29 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
             fb = ptx::mapa(full_bar(stage), 0);
             if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * stage_bytes);
           }
-          auto load = [&](uint32_t dst, const CUtensorMap* map, int x, int y) {
+          unit_boxes(u, kb, [&](bool is_b, uint32_t off, const CUtensorMap* map, int x, int y) {
+            const uint32_t dst = (is_b ? b_dst : a_dst) + off;
             if constexpr (kCtaGroup == 1) ptx::tma_load_2d(dst, map, fb, x, y);
             else ptx::tma_load_2d_pair(dst, map, fb, x, y);
-          };
-          // MN-major (NT) tiles are 64-wide boxes 8 KB apart; K-major (TN)
-          // tiles are one box per operand and MMA.
-          if constexpr (kMnMajor) {
-            load(a_dst, &tmap_a, m0, k0);
-            load(a_dst + 8192, &tmap_a, m0 + 64, k0);
-          } else {
-            load(a_dst, &tmap_a, k0, m0);
-          }
-#pragma unroll
-          for (int j = 0; j < kNumN; ++j) {
-            const int nj = min(n_unit - j * kBN, kBN);
-            if (nj <= 0) break;
-            const int rows = nj / kCtaGroup;
-            const int r0 = nbase + j * kBN + static_cast<int>(cta_rank) * rows;
-            const uint32_t dst = b_dst + j * Cfg::kBytesBPerMma;
-            if constexpr (kMnMajor) {
-#pragma unroll
-              for (int q = 0; q < Cfg::kRowsBPerMma / 64; ++q)
-                if (64 * q < rows) load(dst + 8192 * q, &tmap_b, r0 + 64 * q, k0);
-            } else {
-              load(dst, &tmap_b, k0, r0);
-            }
-          }
+          });
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
+        }
+        // Every load of this unit is issued; the MMA still has up to kStages
+        // k-blocks (and the accumulator drain) before it needs the next
+        // unit's first stages, whose operands come from other A/B panels:
+        // bring those k-blocks into L2 now so their loads do not start cold.
+        if (ok && !it.done(p)) {
+          WorkIter<Cfg::kParts> peek = it;
+          WorkUnit nu;
+          peek.next(p, nu);
+          const int npf = p.k_blocks < kStages ? p.k_blocks : kStages;
+          for (int kb = 0; kb < npf; ++kb)
+            unit_boxes(nu, kb, [&](bool, uint32_t, const CUtensorMap* map, int x, int y) {
+              ptx::tma_prefetch_2d(map, x, y);
+            });
         }
       }
       // Drain: every load this CTA issued must have landed before the CTA
