@@ -371,20 +371,6 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
             phase ^= 1u;
           }
         }
-        // Every load of this unit is issued; the MMA still has up to kStages
-        // k-blocks (and the accumulator drain) before it needs the next
-        // unit's first stages, whose operands come from other A/B panels:
-        // bring those k-blocks into L2 now so their loads do not start cold.
-        if (ok && !it.done(p)) {
-          WorkIter<Cfg::kParts> peek = it;
-          WorkUnit nu;
-          peek.next(p, nu);
-          const int npf = p.k_blocks < kStages ? p.k_blocks : kStages;
-          for (int kb = 0; kb < npf; ++kb)
-            unit_boxes(nu, kb, [&](bool, uint32_t, const CUtensorMap* map, int x, int y) {
-              ptx::tma_prefetch_2d(map, x, y);
-            });
-        }
       }
       // Drain: every load this CTA issued must have landed before the CTA
       // can retire. On the normal path the MMA consumed them all already.

@@ -94,12 +94,6 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
-// Bring one 2D box into L2 (no shared memory, no barrier).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* m, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
-               :: "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y) : "memory");
-}
-
 // 2D tiled load into this CTA's shared memory; completion bytes go to `bar`
 // (this CTA's barrier).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* m, uint32_t bar,
