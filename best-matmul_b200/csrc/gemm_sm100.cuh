@@ -82,9 +82,10 @@ enum StatSlot : int {
   // per tile u < kStatUnits (kStatUnitFields slots each), %globaltimer ns:
   // MMA start, MMA end (last commit issued), epilogue start (accumulator
   // ready), TMEM released, epilogue end (stores issued); then the MMA
-  // thread's cycles waiting for loaded stages during the tile. Written
-  // straight to global memory by the MMA thread and epilogue warp 2.
-  kStatUnit0 = 16, kStatUnits = 6, kStatUnitFields = 6,
+  // thread's cycles waiting for loaded stages during the tile, and its
+  // clock64 cycles from MMA start to MMA end. Written straight to global
+  // memory by the MMA thread and epilogue warp 2.
+  kStatUnit0 = 16, kStatUnits = 6, kStatUnitFields = 7,
   kStatUnitCount = kStatUnit0 + kStatUnitFields * kStatUnits,
   // set-up, %globaltimer ns (warp 1): TMEM allocated, CTA barrier, cluster barrier
   kStatSetupAlloc, kStatSetupSync, kStatSetupCluster,
@@ -415,6 +416,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
 #if defined(BM_KERNEL_STATS)
         if (unit_i < kStatUnits) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i, ptx::globaltimer_ns());
         unit_wait0 = st[kStatMmaFullWait];
+        const long long unit_clk0 = clock64();
 #endif
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
         // MMAs j in [jlo, jhi) of k-block kb from stage stg.
@@ -508,6 +510,8 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (unit_i < kStatUnits) {
           BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 1, ptx::globaltimer_ns());
           BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 5, st[kStatMmaFullWait] - unit_wait0);
+          BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 6,
+                      static_cast<unsigned long long>(clock64() - unit_clk0));
         }
         ++unit_i;
         BM_STAT_PUT(kStatUnitCount, static_cast<unsigned long long>(unit_i));
