@@ -423,19 +423,22 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         auto issue = [&](int stg, int kb, int jlo, int jhi) {
           const uint32_t a_base = sA + stg * Cfg::kBytesA;
           const uint32_t b_base = sB + stg * Cfg::kBytesB;
+          // Consecutive MMAs go to the same accumulator (all K steps of MMA j,
+          // then of MMA j+1): alternating accumulators every MMA measured
+          // ~5 % fewer tensor cycles per k-block on B200.
 #pragma unroll
-          for (int ks = 0; ks < Cfg::kBK / 16; ++ks) {
-            // MN-major: 64 MN-elements per 128-byte row, one row per k; 8-row
-            // swizzle atoms 1 KB apart (SBO); 64-element MN chunks 8 KB apart
-            // (LBO); one K=16 step is 16 rows = 2 KB.
-            // K-major: one 128-byte row (64 k) per M/N row; 8-row atoms 1 KB
-            // apart; one K=16 step advances 32 bytes inside the swizzled row.
-            const uint32_t koff = kMnMajor ? ks * 2048u : ks * 32u;
-            const uint32_t lbo = kMnMajor ? 8192u : 16u;
-            const uint64_t a_desc = ptx::smem_desc_sw128(a_base + koff, lbo, 1024);
+          for (int j = 0; j < kNumN; ++j) {
+            if (j < jlo || j >= jhi || j >= n_mma) continue;
 #pragma unroll
-            for (int j = 0; j < kNumN; ++j) {
-              if (j < jlo || j >= jhi || j >= n_mma) continue;
+            for (int ks = 0; ks < Cfg::kBK / 16; ++ks) {
+              // MN-major: 64 MN-elements per 128-byte row, one row per k; 8-row
+              // swizzle atoms 1 KB apart (SBO); 64-element MN chunks 8 KB apart
+              // (LBO); one K=16 step is 16 rows = 2 KB.
+              // K-major: one 128-byte row (64 k) per M/N row; 8-row atoms 1 KB
+              // apart; one K=16 step advances 32 bytes inside the swizzled row.
+              const uint32_t koff = kMnMajor ? ks * 2048u : ks * 32u;
+              const uint32_t lbo = kMnMajor ? 8192u : 16u;
+              const uint64_t a_desc = ptx::smem_desc_sw128(a_base + koff, lbo, 1024);
               const uint64_t b_desc =
                   ptx::smem_desc_sw128(b_base + j * Cfg::kBytesBPerMma + koff, lbo, 1024);
 #if defined(BM_KERNEL_STATS)
