@@ -77,6 +77,25 @@ def build_harness(force=False, verbose=False) -> str:
     return manifest
 
 
+STATS_LIB = os.path.join(LIB_DIR, "libbmgemm_stats.so")
+
+
+def build_stats_library(force=False, verbose=False) -> str:
+    """Diagnostics build (-DBM_KERNEL_STATS): the same kernels with per-CTA
+    pipeline counters and per-tile timestamps (harness/pipeline_timeline.py)."""
+    os.makedirs(LIB_DIR, exist_ok=True)
+    if not force and not _stale(STATS_LIB, _sources()):
+        return STATS_LIB
+    cmd = [nvcc()] + NVCC_FLAGS + ["-DBM_KERNEL_STATS", "-shared", "-o", STATS_LIB,
+                                   os.path.join(CSRC, "bm_gemm.cu")]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or res.returncode != 0:
+        sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed building {STATS_LIB}")
+    return STATS_LIB
+
+
 def build_all(force=False, verbose=False) -> None:
     build_library(force, verbose)
     build_harness(force, verbose)
@@ -86,6 +105,8 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--stats", action="store_true",
+                    help="also build lib/libbmgemm_stats.so (pipeline counters, diagnostics only)")
     ap.add_argument("--lib-only", action="store_true",
                     help="build only lib/libbmgemm.so (build.sh calls this before the harness)")
     args = ap.parse_args()
@@ -93,4 +114,6 @@ if __name__ == "__main__":
         build_library(args.force, args.verbose)
     else:
         build_all(args.force, args.verbose)
+    if args.stats:
+        build_stats_library(args.force, args.verbose)
     print("built", LIB)
