@@ -91,13 +91,18 @@ cudaError_t launch_variant(const bm_gemm_handle* h, cudaStream_t stream) {
   cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(Cfg::kSmemBytes);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = kCtaGroup;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch: this grid's CTAs may be scheduled while
+  // the previous kernel in the stream finishes; the kernel waits for that
+  // kernel's completion (griddepcontrol.wait) before touching global memory.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, bm::bm_gemm_sm100_kernel<kCtaGroup, kBN, kNumN, kStages, kMn>,
                             h->tmap_a, h->tmap_b, h->tmap_c, h->params);
 }

@@ -276,6 +276,12 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
   if constexpr (kCtaGroup == 2) ptx::cluster_sync();  // peer barriers initialised
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touched only shared memory, TMEM and kernel parameters,
+  // so it may overlap the previous kernel in the stream (launched with
+  // programmatic stream serialization). Global memory (A, B, C, the status
+  // word) is touched only after the previous grid has completed.
+  ptx::griddep_wait();
+  if (threadIdx.x == 0) ptx::griddep_launch_dependents();
 #if defined(BM_KERNEL_STATS)
   unsigned long long st[kNumStats] = {};  // constant indices only: registers
   const long long t_begin = clock64();

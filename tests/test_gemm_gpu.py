@@ -253,3 +253,30 @@ def test_forced_wait_expires_and_reports(bm, cuda):
         g.launch()
         assert g.status() == (bm.BM_OK, 0)
     assert torch.all(c == float(k)).item()
+
+
+def test_dependent_launches_in_one_stream(bm, cuda):
+    """Launches use programmatic dependent launch: the next GEMM's CTAs may be
+    scheduled while the previous kernel runs, and must not touch global memory
+    before it completes. GEMM 2 reads GEMM 1's output as its A operand, back to
+    back on one stream; GEMM 1 is long (K = 4096) but occupies only 2 pairs,
+    so GEMM 2's CTAs are resident early. C1 is NaN-prefilled: any early read
+    shows up in C2. Values are exact: C1 = 4096 * 2^-12 = 1, C2 = 512."""
+    torch = cuda
+    m, n1, k1, n2 = 512, 512, 4096, 512
+    a1 = torch.ones((k1, m), dtype=torch.float16, device="cuda")
+    b1 = torch.full((k1, n1), 2.0 ** -12, dtype=torch.float16, device="cuda")
+    c1 = torch.empty((n1, m), dtype=torch.float16, device="cuda")
+    b2 = torch.ones((n1, n2), dtype=torch.float16, device="cuda")
+    c2 = torch.empty((n2, m), dtype=torch.float16, device="cuda")
+    with bm.Gemm.from_tensors(a1, b1, c1, "NT") as g1, bm.Gemm.from_tensors(c1, b2, c2, "NT") as g2:
+        for rep in range(8):
+            c1.fill_(float("nan"))
+            c2.fill_(float("nan"))
+            g1.launch()
+            g2.launch()
+            g1.launch()  # rewrite C1 while the next iteration's fill waits behind it
+            torch.cuda.synchronize()
+            assert torch.all(c1 == 1.0).item(), f"rep {rep}: C1"
+            assert torch.all(c2 == float(n1)).item(), f"rep {rep}: C2 read C1 too early"
+        assert g1.status() == (bm.BM_OK, 0) and g2.status() == (bm.BM_OK, 0)
