@@ -427,8 +427,12 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
         // MMAs j in [jlo, jhi) of k-block kb from stage stg.
         auto issue = [&](int stg, int kb, int jlo, int jhi) {
-          const uint32_t a_base = sA + stg * Cfg::kBytesA;
-          const uint32_t b_base = sB + stg * Cfg::kBytesB;
+          // Descriptors of the stage's first K step; later steps and MMA 1's B
+          // only move the start address (bits 0-13, 16-byte units), which
+          // never carries out: all of shared memory lies below 256 KB.
+          const uint32_t lbo = kMnMajor ? 8192u : 16u;
+          const uint64_t a_desc0 = ptx::smem_desc_sw128(sA + stg * Cfg::kBytesA, lbo, 1024);
+          const uint64_t b_desc0 = ptx::smem_desc_sw128(sB + stg * Cfg::kBytesB, lbo, 1024);
           // Consecutive MMAs go to the same accumulator (all K steps of MMA j,
           // then of MMA j+1): alternating accumulators every MMA measured
           // ~5 % fewer tensor cycles per k-block on B200.
@@ -443,10 +447,8 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
               // K-major: one 128-byte row (64 k) per M/N row; 8-row atoms 1 KB
               // apart; one K=16 step advances 32 bytes inside the swizzled row.
               const uint32_t koff = kMnMajor ? ks * 2048u : ks * 32u;
-              const uint32_t lbo = kMnMajor ? 8192u : 16u;
-              const uint64_t a_desc = ptx::smem_desc_sw128(a_base + koff, lbo, 1024);
-              const uint64_t b_desc =
-                  ptx::smem_desc_sw128(b_base + j * Cfg::kBytesBPerMma + koff, lbo, 1024);
+              const uint64_t a_desc = a_desc0 + (koff >> 4);
+              const uint64_t b_desc = b_desc0 + ((j * Cfg::kBytesBPerMma + koff) >> 4);
 #if defined(BM_KERNEL_STATS)
               if (st[kStatMmaFirst] == 0) st[kStatMmaFirst] = ptx::globaltimer_ns();
 #endif
