@@ -1,17 +1,18 @@
 """Per-tile pipeline timeline of one GEMM launch (diagnostics).
 
     python best-matmul_b200/build.py --lib-only --stats
-    python best-matmul_b200/harness/pipeline_timeline.py [--size 4096] [--layout TN]
-           [--variant 0] [--split auto|none] [--reps 5]
+    python best-matmul_b200/harness/pipeline_timeline.py [--size 4096 | --m M --n N --k K]
+           [--layout TN] [--variant 0] [--split auto|none] [--reps 5]
 
 Loads lib/libbmgemm_stats.so (the kernels built with -DBM_KERNEL_STATS), which
 writes, per CTA, %globaltimer stamps of set-up, of every tile's MMA start and
 end, of the epilogue's start, TMEM release and last store, plus the MMA
 thread's clock64 cycles and data-wait cycles per tile. Prints, per tile index,
-the means over the pair leaders, and the MMA-thread cycles against the ideal
-of 1024 cycles per 64-deep k-block of a 256x512 pair tile (8 MMAs of
-256x256x16 per k-block, 128 cycles each per SM). The stats build is for
-diagnosis only; its absolute times include its own bookkeeping.
+the means over the cluster leaders, and the MMA-thread cycles against the
+tensor-pipe ideal of a whole tile: per 64-deep k-block, (tile rows per CTA x
+tile columns x 64) multiply-adds at 4096 per cycle per SM (1024 cycles for the
+256x512 pair tile). The stats build is for diagnosis only; its absolute times
+include its own bookkeeping.
 """
 from __future__ import annotations
 
@@ -36,6 +37,9 @@ NUM_STATS = SETUP_CLUSTER + 1
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--size", type=int, default=4096)
+    ap.add_argument("--m", type=int, default=0)
+    ap.add_argument("--n", type=int, default=0)
+    ap.add_argument("--k", type=int, default=0)
     ap.add_argument("--layout", default="TN")
     ap.add_argument("--variant", type=int, default=0)
     ap.add_argument("--split", choices=["auto", "none"], default="auto")
@@ -49,7 +53,7 @@ def main():
     lib.bm_gemm_debug_attach_stats.restype = ctypes.c_int
     lib.bm_gemm_debug_attach_stats.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
 
-    m = n = k = args.size
+    m, n, k = (args.m or args.size), (args.n or args.size), (args.k or args.size)
     a, b, c = bm.alloc_operands(m, n, k, args.layout, mode=4, seed=0)
     g = bm.Gemm.from_tensors(a, b, c, args.layout, variant=args.variant)
     g.set_split(bm.SPLIT_AUTO if args.split == "auto" else bm.SPLIT_NONE)
@@ -82,6 +86,8 @@ def main():
           f"{us((lead[:, SETUP_ALLOC] - t0).mean()):.2f}, CTA barrier {us((lead[:, SETUP_SYNC] - t0).mean()):.2f}, "
           f"cluster barrier {us((lead[:, SETUP_CLUSTER] - t0).mean()):.2f}, first MMA {us((lead[:, MMA_FIRST] - t0).mean()):.2f}")
     kb = (k + 63) // 64
+    tile_m, tile_n = info["tile"][0], info["tile"][1]
+    ideal_kb = (tile_m // cg) * tile_n * 64 // 4096  # MMA cycles per k-block per SM
     for u in range(UNITS):
         sel = lead[lead[:, UNIT_COUNT] > u]
         if len(sel) == 0:
@@ -90,8 +96,8 @@ def main():
         ms, me, es, er, ee = (sel[:, base + i] - t0 for i in range(5))
         wait, cyc = sel[:, base + 5], sel[:, base + 6]
         print(f"tile {u}: {len(sel)} pairs | MMA {us(ms.mean()):.1f} -> {us(me.mean()):.1f} us | "
-              f"MMA-thread cycles {cyc.mean():.0f} (ideal {kb * 1024} for a whole 256x512 tile: "
-              f"{kb * 1024 / cyc.mean():.3f}), data waits {wait.mean():.0f} | accumulator ready "
+              f"MMA-thread cycles {cyc.mean():.0f} (whole-tile ideal {kb * ideal_kb}: "
+              f"{kb * ideal_kb / cyc.mean():.3f}), data waits {wait.mean():.0f} | accumulator ready "
               f"+{us((es - me).mean()):.1f} us, TMEM held {us((er - es).mean()):.2f} us, stores issued "
               f"+{us((ee - er).mean()):.2f} us | last store {us(ee.max()):.1f} us")
     g.close()
