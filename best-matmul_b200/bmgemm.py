@@ -47,7 +47,6 @@ VARIANT_TILES = {1: (256, 256, 6), 2: (128, 256, 4), 3: (128, 128, 6), 4: (256, 
                  5: (256, 512, 4)}
 
 DEBUG_EPILOGUE_WAITS_NEVER = 1
-DEBUG_SPLIT_FLAGS_NEVER = 2
 
 SPLIT_NONE = 0
 SPLIT_AUTO = 1
@@ -81,8 +80,7 @@ class ScheduleInfo(ctypes.Structure):
         ("whole_tiles", ctypes.c_int), ("split_tiles", ctypes.c_int),
         ("split_parts", ctypes.c_int), ("split_clusters", ctypes.c_int),
         ("grid_clusters", ctypes.c_int), ("resident_clusters", ctypes.c_int),
-        ("split_cols", ctypes.c_int), ("k_split_clusters", ctypes.c_int),
-        ("workspace_bytes", ctypes.c_uint64),
+        ("split_cols", ctypes.c_int),
     ]
 
 

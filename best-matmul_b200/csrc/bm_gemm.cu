@@ -78,8 +78,6 @@ struct bm_gemm_handle {
   int max_clusters;  // resident clusters of this variant on this device
   int parts;         // column parts per tile the variant can split into (1: none)
   int split_mode;    // enum bm_split_mode
-  void* d_workspace;       // K-split flags + partial tiles (null when nothing is split)
-  size_t workspace_bytes;
 };
 
 namespace {
@@ -225,56 +223,14 @@ int split_parts(int variant) {
                                                                    : 1;
 }
 
-// K-split pieces are at least this many k-blocks (pieces of one tile stay few).
-constexpr int kMinSplitKBlocks = 16;
-
-// Skinny problems (M <= 128) run on 1-CTA tiles and are bound by HBM: with
-// fewer tiles than SMs, each SM's loads in flight (capped by its shared
-// memory) limit the bandwidth, so the K range is split over all SMs.
-bool k_split_candidate(const bm_gemm_handle* h) {
-  return h->split_mode == BM_SPLIT_AUTO && h->cta_group == 1 && h->params.m <= 128;
-}
-
-// (Re)plan the schedule and size the K-split workspace:
-// [flags: sk_clusters x kEpiWarps uint32, 256-byte aligned]
-// [partials: sk_clusters x tile_m x tile_n FP32]. Flags start at zero; every
-// owner clears the flags it consumed.
-int apply_plan(bm_gemm_handle* h) {
+void apply_plan(bm_gemm_handle* h) {
   GemmParams& p = h->params;
-  const bm::Plan pl =
-      k_split_candidate(h)
-          ? bm::plan_k_split(p.num_tiles, p.k_blocks, h->max_clusters, kMinSplitKBlocks)
-          : bm::plan_schedule(p.num_tiles, h->parts, h->max_clusters,
-                              h->split_mode == BM_SPLIT_AUTO ? 1 : 0);
-  size_t flag_bytes = 0, need = 0;
-  if (pl.sk_clusters > 0) {
-    flag_bytes = (static_cast<size_t>(pl.sk_clusters) * bm::kEpiWarps * sizeof(uint32_t) + 255) &
-                 ~static_cast<size_t>(255);
-    need = flag_bytes + static_cast<size_t>(pl.sk_clusters) * h->tile_m * h->tile_n * sizeof(float);
-  }
-  if (need > h->workspace_bytes || (need == 0 && h->d_workspace)) {
-    if (h->d_workspace) cudaFree(h->d_workspace);
-    h->d_workspace = nullptr;
-    h->workspace_bytes = 0;
-    if (need > 0) {
-      if (cudaMalloc(&h->d_workspace, need) != cudaSuccess) {
-        h->d_workspace = nullptr;
-        return BM_ERR_CUDA;
-      }
-      h->workspace_bytes = need;
-    }
-  }
-  if (need > 0 && cudaMemset(h->d_workspace, 0, flag_bytes) != cudaSuccess) return BM_ERR_CUDA;
+  const bm::Plan pl = bm::plan_schedule(p.num_tiles, h->parts, h->max_clusters,
+                                        h->split_mode == BM_SPLIT_AUTO ? 1 : 0);
   p.dp_tiles = pl.dp_tiles;
   p.tail_parts = pl.tail_parts;
   p.tail_clusters = pl.tail_clusters;
-  p.sk_clusters = pl.sk_clusters;
-  p.sk_total = pl.sk_total;
-  p.sk_flags = need ? static_cast<uint32_t*>(h->d_workspace) : nullptr;
-  p.sk_partials = need ? reinterpret_cast<float*>(static_cast<char*>(h->d_workspace) + flag_bytes)
-                       : nullptr;
   h->grid = pl.grid_clusters * h->cta_group;
-  return BM_OK;
 }
 
 // Automatic variant choice: estimated throughput = (relative per-tile
@@ -435,6 +391,7 @@ int bm_gemm_prepare(const bm_gemm_desc* d, bm_gemm_handle** out) {
   h->max_clusters = max_clusters;
   h->parts = split_parts(v);
   h->split_mode = BM_SPLIT_AUTO;
+  apply_plan(h);
 
   if (cudaMalloc(reinterpret_cast<void**>(&h->d_status), sizeof(uint32_t)) != cudaSuccess) {
     delete h;
@@ -446,11 +403,6 @@ int bm_gemm_prepare(const bm_gemm_desc* d, bm_gemm_handle** out) {
     return BM_ERR_CUDA;
   }
   p.status = h->d_status;
-  rc = apply_plan(h);
-  if (rc != BM_OK) {
-    bm_gemm_destroy(h);
-    return rc;
-  }
   *out = h;
   return BM_OK;
 }
@@ -488,13 +440,6 @@ int bm_gemm_status(bm_gemm_handle* h, uint32_t* bits) {
   if (cudaMemcpy(&v, h->d_status, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess)
     return BM_ERR_CUDA;
   if (cudaMemset(h->d_status, 0, sizeof(uint32_t)) != cudaSuccess) return BM_ERR_CUDA;
-  // A launch that gave up may have left K-split flags raised: clear them so
-  // the next launch cannot read a stale partial.
-  if (v && h->params.sk_flags &&
-      cudaMemset(h->params.sk_flags, 0,
-                 static_cast<size_t>(h->params.sk_clusters) * bm::kEpiWarps * sizeof(uint32_t)) !=
-          cudaSuccess)
-    return BM_ERR_CUDA;
   if (bits) *bits = v;
   return v ? BM_ERR_DEVICE_TIMEOUT : BM_OK;
 }
@@ -508,18 +453,9 @@ int bm_gemm_set_debug(bm_gemm_handle* h, uint64_t timeout_ns, uint32_t flags) {
 
 int bm_gemm_set_split(bm_gemm_handle* h, int mode) {
   if (!h || (mode != BM_SPLIT_NONE && mode != BM_SPLIT_AUTO)) return BM_ERR_INVALID_ARGUMENT;
-  // The K-split workspace may be freed or replaced: nothing of this handle
-  // may be in flight.
-  int prev = 0;
-  if (cudaGetDevice(&prev) != cudaSuccess) return BM_ERR_CUDA;
-  if (prev != h->device && cudaSetDevice(h->device) != cudaSuccess) return BM_ERR_CUDA;
-  int rc = BM_ERR_CUDA;
-  if (cudaDeviceSynchronize() == cudaSuccess) {
-    h->split_mode = mode;
-    rc = apply_plan(h);
-  }
-  if (prev != h->device) cudaSetDevice(prev);
-  return rc;
+  h->split_mode = mode;
+  apply_plan(h);
+  return BM_OK;
 }
 
 int bm_gemm_query_schedule(const bm_gemm_handle* h, bm_schedule_info* info) {
@@ -533,8 +469,6 @@ int bm_gemm_query_schedule(const bm_gemm_handle* h, bm_schedule_info* info) {
   info->grid_clusters = h->grid / h->cta_group;
   info->resident_clusters = h->max_clusters;
   info->split_cols = h->parts > 1 ? bm::kSplitCols : 0;
-  info->k_split_clusters = p.sk_clusters;
-  info->workspace_bytes = static_cast<uint64_t>(h->workspace_bytes);
   return BM_OK;
 }
 
@@ -551,7 +485,6 @@ int bm_gemm_debug_attach_stats(bm_gemm_handle* h, void* stats) {
 void bm_gemm_destroy(bm_gemm_handle* h) {
   if (!h) return;
   if (h->d_status) cudaFree(h->d_status);
-  if (h->d_workspace) cudaFree(h->d_workspace);
   delete h;
 }
 
@@ -714,7 +647,6 @@ extern "C" int bm_gemm_run_noalloc(const bm_gemm_desc* d, void* stream, uint32_t
   p.dp_tiles = p.num_tiles;  // whole tiles, one wave after another
   p.tail_parts = 0;
   p.tail_clusters = 0;
-  p.sk_clusters = 0;  // no K split: its workspace would not fit the static scratch
   const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
   h.grid = clusters * h.cta_group;
 

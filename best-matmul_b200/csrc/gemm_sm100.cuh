@@ -51,7 +51,6 @@ enum : uint32_t {
 // Debug flags (kernel parameter).
 enum : uint32_t {
   kDebugEpilogueWaitsNever = 1u << 0,  // epilogue first waits on a barrier nothing signals
-  kDebugSplitFlagsNever = 1u << 1,     // K-split contributors never raise their flags
 };
 
 struct GemmParams {
@@ -71,15 +70,6 @@ struct GemmParams {
   int dp_tiles;
   int tail_parts;
   int tail_clusters;
-  // K split (1-CTA variants, memory-bound grids): the k-blocks of tiles
-  // [dp_tiles, num_tiles) (sk_total, tile-major) split over clusters
-  // [0, sk_clusters); 0 = none. Partial tiles meet in sk_partials, one
-  // kTileM x kTileN FP32 slot per cluster; sk_flags holds kEpiWarps ready
-  // flags per cluster (0 = empty; the consuming owner clears them).
-  int sk_clusters;
-  long long sk_total;
-  float* sk_partials;
-  uint32_t* sk_flags;
 };
 
 // Opt-in pipeline counters (build with -DBM_KERNEL_STATS): per CTA, cycles
@@ -163,8 +153,6 @@ struct GemmConfig {
   // after the other: tempty_bar(0) frees columns [0, 256), tempty_bar(1)
   // columns [256, 512) (kAccStages == 1 leaves the second barrier free).
   static constexpr bool kHalfRelease = kTailSplit;
-  // 1-CTA variants (two accumulators) may split K across clusters.
-  static constexpr bool kKSplit = (kCtaGroup == 1);
   static_assert(!kHalfRelease || (kAccStages == 1 && kTileN == 512), "half release layout");
   static constexpr int kParts = kTailSplit ? kTileN / kSplitCols : 1;
 
@@ -362,7 +350,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           stage_bytes += is_b ? (kMnMajor ? 8192u : static_cast<uint32_t>(Cfg::kBytesBPerMma))
                               : (kMnMajor ? 8192u : static_cast<uint32_t>(Cfg::kBytesA));
         });
-        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!BM_WAIT(empty_bar(stage), phase ^ 1u, p.timeout_ns, abort_flag, kStatProdWait, kStatProdWaits)) {
             fail(kStatusProducerTimeout);
             ok = false;
@@ -465,7 +453,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
               if (st[kStatMmaFirst] == 0) st[kStatMmaFirst] = ptx::globaltimer_ns();
 #endif
               ptx::mma_f16<kCtaGroup>(d_tmem + static_cast<uint32_t>(j * kBN), a_desc, b_desc,
-                                      j == 0 ? idesc0 : idesc1, (kb > u.kb0 || ks > 0) ? 1u : 0u);
+                                      j == 0 ? idesc0 : idesc1, (kb > 0 || ks > 0) ? 1u : 0u);
             }
           }
         };
@@ -477,13 +465,13 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           st[kStatKBlocks] += 1;
 #endif
         };
-        int kb = u.kb0;
+        int kb = 0;
         if constexpr (Cfg::kHalfRelease) {
           // The epilogue hands back TMEM columns [0, 256) first: run MMA 0 of
           // the first kStages k-blocks (already loaded while the previous
           // tile drained) into them, then, once [256, 512) is free too, MMA 1
           // of the same k-blocks, releasing each stage after both.
-          const int pre = u.kb0 + (u.kb1 - u.kb0 < kStages ? u.kb1 - u.kb0 : kStages);
+          const int pre = p.k_blocks < kStages ? p.k_blocks : kStages;
           const int stage0 = stage;
           for (; kb < pre; ++kb) {
             if (!BM_WAIT(full_bar(stage), phase, p.timeout_ns, abort_flag, kStatMmaFullWait, kStatMmaFullWaits)) {
@@ -505,13 +493,13 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
           }
           ptx::tc_fence_after();
           int s2 = stage0;
-          for (int k2 = u.kb0; k2 < pre; ++k2) {
+          for (int k2 = 0; k2 < pre; ++k2) {
             issue(s2, k2, 1, kNumN);
             release_stage(s2);
             if (++s2 == kStages) s2 = 0;
           }
         }
-        for (; kb < u.kb1; ++kb) {
+        for (; kb < p.k_blocks; ++kb) {
           if (!BM_WAIT(full_bar(stage), phase, p.timeout_ns, abort_flag, kStatMmaFullWait, kStatMmaFullWaits)) {
             fail(kStatusMmaTimeout);
             ok = false;
@@ -670,89 +658,7 @@ bm_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
         if (put) BM_STAT_PUT(kStatUnit0 + kStatUnitFields * unit_i + 3, ptx::globaltimer_ns());
 #endif
       };
-      bool split_done = false;
-      if constexpr (Cfg::kKSplit) {
-        if (u.kind != kUnitFull) {
-          // K-split piece. Partial slots: one kTileM x kTileN FP32 tile per
-          // cluster; this warp's part is cpw chunks of 32 x 32, each stored
-          // as 8 x (32 lanes x float4), so every store and load is coalesced;
-          // an owner's warp reads exactly what the same warp of a
-          // contributor cluster wrote.
-          auto slot = [&](int cluster, int cc) -> float4* {
-            const size_t off = static_cast<size_t>(cluster) * (Cfg::kTileM * Cfg::kTileN) +
-                               static_cast<size_t>(ew * Cfg::kChunksPerWarp + cc) * 1024;
-            return reinterpret_cast<float4*>(p.sk_partials + off);
-          };
-          auto flag = [&](int cluster) -> uint32_t* {
-            return p.sk_flags + static_cast<size_t>(cluster) * kEpiWarps + ew;
-          };
-          if (u.kind == kUnitOwner) {
-            // Contributors ran these pieces first in their ranges; the
-            // waits are normally satisfied at once.
-            for (int j = cluster_id + 1; j < u.contrib_end && ok; ++j) {
-              if (!ptx::bm_wait_flag(flag(j), p.timeout_ns, abort_flag)) {
-                if (lane == 0) fail(kStatusEpilogueTimeout);
-                ok = false;
-              }
-            }
-            if (!ok) break;
-          }
-#pragma unroll 1
-          for (int cc = 0; cc < cpw; ++cc) {
-            uint32_t r[32];
-            uint32_t (&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[0]);
-            uint32_t (&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[16]);
-            const int ch = chunk_of(cc);
-            ptx::tmem_ld_32x32b_x16(t_acc + static_cast<uint32_t>(ch * 32), r0);
-            ptx::tmem_ld_32x32b_x16(t_acc + static_cast<uint32_t>(ch * 32 + 16), r1);
-            ptx::tmem_wait_ld();
-            if (u.kind == kUnitContrib) {
-              float4* dst = slot(cluster_id, cc);
-#pragma unroll
-              for (int q = 0; q < 8; ++q)
-                __stcg(dst + q * 32 + lane,
-                       make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                   __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
-            } else {
-              // Fixed order (increasing k ranges): the bits do not depend on timing.
-              for (int j = cluster_id + 1; j < u.contrib_end; ++j) {
-                const float4* src = slot(j, cc);
-                float4 v[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) v[q] = __ldcg(src + q * 32 + lane);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                  r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + v[q].x);
-                  r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + v[q].y);
-                  r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + v[q].z);
-                  r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + v[q].w);
-                }
-              }
-              uint32_t hc[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) hc[i] = pack_pair(r[2 * i], r[2 * i + 1]);
-              stage_store(hc, row0, col0, ch, last, cc);
-            }
-          }
-          release_tmem();
-          if (u.kind == kUnitContrib) {
-            // Publish: every lane's partial stores, then this warp's flag.
-            __threadfence();
-            __syncwarp();
-            if (lane == 0 && !(p.debug & kDebugSplitFlagsNever)) ptx::st_release_gpu(flag(cluster_id), 1u);
-          } else {
-            // Consumed: clear the contributors' flags for the next launch
-            // (stream order puts that launch's stores after these).
-            __syncwarp();
-            if (lane == 0)
-              for (int j = cluster_id + 1; j < u.contrib_end; ++j) *flag(j) = 0u;
-          }
-          split_done = true;
-        }
-      }
-      if (split_done) {
-        // K-split piece handled above.
-      } else if (last) {
+      if (last) {
         // No next tile waits for TMEM: store each chunk as soon as it is
         // packed, so TMEM reads and stores overlap (16-column TMEM loads,
         // double-buffered).

@@ -101,35 +101,6 @@ __device__ __forceinline__ bool bm_wait(uint32_t bar, uint32_t parity, uint64_t 
   }
 }
 
-// ------------------------------------------------- global-memory flags
-// Flags CTAs of one resident grid use to hand partial tiles to each other
-// (K split). The writer publishes with a release store after its data
-// stores; the reader polls with acquire loads, so data written before the
-// release is visible to loads issued after the acquire.
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
-}
-
-// Bounded poll until *flag != 0. Returns false when `timeout_ns` elapsed or
-// `*abort_flag` became non-zero.
-__device__ __forceinline__ bool bm_wait_flag(const uint32_t* flag, uint64_t timeout_ns,
-                                             const volatile uint32_t* abort_flag) {
-  if (ld_acquire_gpu(flag) != 0u) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    __nanosleep(64);
-    if (ld_acquire_gpu(flag) != 0u) return true;
-    if (*abort_flag != 0u) return false;
-    if (globaltimer_ns() - t0 > timeout_ns) return false;
-  }
-}
-
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -12,9 +12,7 @@
  *
  * Conventions
  *  - All pointers passed as A/B/C are device pointers owned by the caller.
- *    A handle owns its tensor maps, a 4-byte device status word and, when
- *    its schedule splits K (skinny problems, see bm_gemm_set_split), an FP32
- *    workspace for partial tiles.
+ *    A handle owns only its tensor maps and a 4-byte device status word.
  *  - Functions return BM_OK (0) or a BM_ERR_* code; nothing calls exit().
  *    (The reference calls std::exit on failure, tma_wgmma_adapter.cuh:122-125.)
  *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
@@ -127,8 +125,7 @@ int bm_gemm_status(bm_gemm_handle* handle, uint32_t* device_bits);
 
 /* Test hooks: bound on every in-kernel wait (default 2 s) and debug flags
  * (bit 0: the epilogue first waits on a barrier that nothing signals, so the
- * wait must expire and be reported; bit 1: K-split contributors never raise
- * their ready flags, so the owners' waits must expire and be reported). */
+ * wait must expire and be reported). */
 int bm_gemm_set_debug(bm_gemm_handle* handle, uint64_t timeout_ns, uint32_t debug_flags);
 
 void bm_gemm_destroy(bm_gemm_handle* handle);
@@ -141,15 +138,11 @@ void bm_gemm_destroy(bm_gemm_handle* handle);
  *                 left for the last wave are at most half the resident
  *                 clusters, they are cut into 256-column halves (full K
  *                 range, one N = 256 MMA per K step) that twice as many
- *                 clusters share (2-CTA 256x512 variant). Each output element
- *                 is still one MMA chain over all of K in the same order:
- *                 the bits equal the whole-tile result, nothing is allocated.
- *                 Skinny problems (M <= 128, HBM-bound, 1-CTA tiles) with
- *                 fewer tiles than SMs instead split K over all SMs: partial
- *                 tiles are summed in a fixed order through an FP32 workspace
- *                 the handle allocates (results differ from whole tiles only
- *                 by FP32 summation order and repeat bit for bit).
- *   BM_SPLIT_NONE whole tiles only. */
+ *                 clusters share. Only the 2-CTA 256x512 variant splits.
+ *   BM_SPLIT_NONE whole tiles only.
+ * Each output element is still computed by one MMA chain over all of K in the
+ * same order, so both modes give the same bits; nothing is allocated and no
+ * CTA waits on another. */
 enum bm_split_mode { BM_SPLIT_NONE = 0, BM_SPLIT_AUTO = 1 };
 
 typedef struct bm_schedule_info {
@@ -160,14 +153,10 @@ typedef struct bm_schedule_info {
   int grid_clusters;     /* clusters launched */
   int resident_clusters; /* clusters that fit on the device at once */
   int split_cols;        /* columns per part (0: variant never splits) */
-  int k_split_clusters;  /* clusters sharing the K range of the tiles (0: no K split) */
-  uint64_t workspace_bytes; /* device workspace held by the handle */
 } bm_schedule_info;
 
-/* Re-plan a prepared handle's schedule (mode: enum bm_split_mode). May
- * allocate or free the handle's workspace, so it synchronises the device
- * first: never call it while a launch of this handle is in flight or being
- * captured. Takes effect from the next bm_gemm_launch. */
+/* Re-plan a prepared handle's schedule (mode: enum bm_split_mode). Host-side
+ * only: takes effect from the next bm_gemm_launch. */
 int bm_gemm_set_split(bm_gemm_handle* handle, int mode);
 
 /* Schedule of a prepared handle. */

@@ -14,18 +14,9 @@
 //   4. no cluster computes more parts of split tiles than the plan's run;
 //   5. the grid covers every cluster that has work, within the resident ones;
 //   6. done() is true exactly when next() has nothing left.
-// K split (plan_k_split, memory-bound grids with fewer tiles than clusters):
-//   7. every k-block of every tile is computed exactly once, every tile is
-//      stored exactly once (a full or an owner piece);
-//   8. an owner's contributors [owner + 1, contrib_end) are exactly the
-//      clusters holding contributor pieces of its tile;
-//   9. a contributor piece is its cluster's first piece and an owner piece
-//      its last (so owners only wait on work run first: no deadlock), and
-//      each cluster has at most one contributor piece (one partial slot).
 // Exit status 0 when every case holds.
 #include <cstdio>
 #include <cstdlib>
-#include <string>
 #include <vector>
 
 #include "schedule.cuh"
@@ -33,8 +24,7 @@
 namespace {
 
 struct Params {
-  int k_blocks, dp_tiles, tail_parts, tail_clusters, sk_clusters;
-  long long sk_total;
+  int dp_tiles, tail_parts, tail_clusters;
 };
 
 int g_fail = 0;
@@ -47,7 +37,7 @@ void fail(const char* what, int t, int q, int c, int split) {
 template <int Q>
 bool check_case(int tiles, int clusters, int split, bool print) {
   const bm::Plan pl = bm::plan_schedule(tiles, Q, clusters, split);
-  const Params p{1, pl.dp_tiles, pl.tail_parts, pl.tail_clusters, pl.sk_clusters, pl.sk_total};
+  const Params p{pl.dp_tiles, pl.tail_parts, pl.tail_clusters};
   const int before = g_fail;
   const bool splits = pl.tail_parts > 0;
   if (splits && pl.dp_tiles % clusters != 0) fail("whole tiles not full waves", tiles, Q, clusters, split);
@@ -93,77 +83,6 @@ bool check_case(int tiles, int clusters, int split, bool print) {
   return g_fail == before;
 }
 
-bool check_k_split(int tiles, int kb, int clusters, int min_kb, bool print) {
-  const bm::Plan pl = bm::plan_k_split(tiles, kb, clusters, min_kb);
-  const Params p{kb, pl.dp_tiles, 0, 0, pl.sk_clusters, pl.sk_total};
-  const int before = g_fail;
-  auto bad = [&](const char* what) {
-    if (g_fail < 20)
-      std::printf("FAIL %s (k-split tiles=%d kb=%d clusters=%d min_kb=%d)\n", what, tiles, kb, clusters, min_kb);
-    ++g_fail;
-  };
-  if (pl.grid_clusters > clusters || pl.sk_clusters > pl.grid_clusters) bad("grid");
-  if (pl.sk_clusters > 0 && (pl.dp_tiles != 0 || pl.sk_total != static_cast<long long>(tiles) * kb)) bad("plan");
-  std::vector<int> cover(static_cast<size_t>(tiles) * kb, 0), stores(tiles, 0), owner_of(tiles, -1),
-      owner_end(tiles, -1);
-  std::vector<std::vector<int>> contrib_of(tiles);
-  for (int c = 0; c < pl.grid_clusters; ++c) {
-    bm::WorkIter<1> it(p, c, pl.grid_clusters);
-    bm::WorkUnit u;
-    std::vector<bm::WorkUnit> units;
-    while (it.next(p, u)) units.push_back(u);
-    int contribs = 0;
-    for (size_t i = 0; i < units.size(); ++i) {
-      const bm::WorkUnit& w = units[i];
-      if (print)
-        std::printf("cluster %d: tile %d k [%d,%d) kind %d contrib_end %d\n", c, w.tile, w.kb0, w.kb1, w.kind,
-                    w.contrib_end);
-      if (w.tile < 0 || w.tile >= tiles || w.kb0 < 0 || w.kb1 > kb || w.kb0 >= w.kb1) {
-        bad("piece out of range");
-        continue;
-      }
-      for (int k = w.kb0; k < w.kb1; ++k) cover[static_cast<size_t>(w.tile) * kb + k] += 1;
-      if (w.kind == bm::kUnitFull) {
-        if (w.kb0 != 0 || w.kb1 != kb) bad("full piece not whole");
-        stores[w.tile] += 1;
-      } else if (w.kind == bm::kUnitOwner) {
-        if (w.kb0 != 0 || w.kb1 >= kb) bad("owner range");
-        if (i + 1 != units.size()) bad("owner piece not last");
-        stores[w.tile] += 1;
-        owner_of[w.tile] = c;
-        owner_end[w.tile] = w.contrib_end;
-      } else {
-        if (w.kb0 == 0) bad("contributor starts at 0");
-        if (i != 0) bad("contributor piece not first");
-        ++contribs;
-        contrib_of[w.tile].push_back(c);
-      }
-    }
-    if (contribs > 1) bad("more than one contributor piece");
-  }
-  for (int t = 0; t < tiles; ++t) {
-    for (int k = 0; k < kb; ++k)
-      if (cover[static_cast<size_t>(t) * kb + k] != 1) {
-        bad("k-block not covered exactly once");
-        break;
-      }
-    if (stores[t] != 1) bad("tile not stored exactly once");
-    if (!contrib_of[t].empty()) {
-      if (owner_of[t] < 0) {
-        bad("contributions without owner");
-        continue;
-      }
-      const int o = owner_of[t], n = owner_end[t] - (o + 1);
-      bool same = n == static_cast<int>(contrib_of[t].size());
-      for (int i = 0; same && i < n; ++i) same = contrib_of[t][i] == o + 1 + i;
-      if (!same) bad("owner's contributor list");
-    } else if (owner_of[t] >= 0 && owner_end[t] != owner_of[t] + 1) {
-      bad("owner expects missing contributors");
-    }
-  }
-  return g_fail == before;
-}
-
 template <int Q>
 long long sweep() {
   long long n = 0;
@@ -179,14 +98,6 @@ long long sweep() {
 }  // namespace
 
 int main(int argc, char** argv) {
-  if (argc == 6 && std::string(argv[1]) == "ksplit") {
-    const int t = std::atoi(argv[2]), kb = std::atoi(argv[3]), c = std::atoi(argv[4]), mk = std::atoi(argv[5]);
-    const bool ok = check_k_split(t, kb, c, mk, true);
-    const bm::Plan pl = bm::plan_k_split(t, kb, c, mk);
-    std::printf("plan sk_clusters=%d sk_total=%lld grid=%d est=%.4f\n", pl.sk_clusters, pl.sk_total,
-                pl.grid_clusters, pl.est);
-    return ok ? 0 : 1;
-  }
   if (argc == 5) {
     const int t = std::atoi(argv[1]), q = std::atoi(argv[2]), c = std::atoi(argv[3]), s = std::atoi(argv[4]);
     bool ok = false;
@@ -201,14 +112,7 @@ int main(int argc, char** argv) {
                 pl.tail_parts, pl.tail_clusters, pl.grid_clusters, pl.est);
     return ok ? 0 : 1;
   }
-  long long n = sweep<1>() + sweep<2>() + sweep<4>();
-  for (int clusters : {1, 2, 3, 7, 16, 37, 74, 148})
-    for (int kb : {1, 2, 3, 5, 8, 31, 64, 128})
-      for (int tiles = 1; tiles <= clusters; ++tiles)
-        for (int min_kb : {0, 1, 4, 16}) {
-          check_k_split(tiles, kb, clusters, min_kb, false);
-          ++n;
-        }
+  const long long n = sweep<1>() + sweep<2>() + sweep<4>();
   std::printf("%lld cases, %d failures\n", n, g_fail);
   return g_fail == 0 ? 0 : 1;
 }

@@ -65,25 +65,3 @@ def test_small_remainder_is_halved(checker):
 def test_fewer_tiles_than_clusters(checker):
     """2048^3 pair tiles: 32 tiles, their 64 halves over 64 pairs."""
     assert _plan(checker, 32, 2, 74) == (0, 64, 64, 64)
-
-
-def _plan_ksplit(checker, tiles, kb, clusters, min_kb):
-    out = subprocess.run([checker, "ksplit", str(tiles), str(kb), str(clusters), str(min_kb)],
-                         capture_output=True, text=True)
-    assert out.returncode == 0, out.stdout
-    m = re.search(r"plan sk_clusters=(\d+) sk_total=(\d+) grid=(\d+)", out.stdout)
-    return tuple(int(x) for x in m.groups()), out.stdout
-
-
-def test_skinny_k_split(checker):
-    """128 x 28672 x 8192 on 1-CTA 128x256 tiles: 112 tiles, 128 k-blocks each,
-    split over all 148 SMs (about 97 k-blocks each); every piece checked."""
-    (skc, total, grid), text = _plan_ksplit(checker, 112, 128, 148, 16)
-    assert (skc, total, grid) == (148, 112 * 128, 148)
-    assert text.count("kind 2") <= 148  # at most one contributor piece per cluster
-
-
-def test_k_split_needs_enough_k(checker):
-    """Short K (8 k-blocks, pieces of >= 16): nothing to split."""
-    (skc, _, grid), _ = _plan_ksplit(checker, 112, 8, 148, 16)
-    assert skc == 0 and grid == 112

@@ -109,82 +109,3 @@ def test_bench_shape_schedule_and_bits(bm, orc, cuda, layout):
     ref = orc.entries_f64(k, layout, ha, lda, hb, ldb, rows, cols)
     bad, merr, _ = orc.check(_bits(c)[cols, rows], ref, k, RTOL, ATOL)
     assert bad == 0, f"{bad} bad samples, max err {merr}"
-
-
-# ----------------------------------------------------------- K split (skinny)
-@pytest.mark.parametrize("layout", ["NT", "TN"])
-def test_k_split_exact_integers(bm, orc, cuda, layout):
-    """Skinny M = 128: 8 tiles of 128x256, 40 k-blocks each, K split over 20
-    SMs (several contributors per tile). Integer inputs, NaN-prefilled C, two
-    launches: every element bit for bit against the exact result."""
-    torch = cuda
-    m, n, k = 128, 2048, 64 * 40
-    lda, ldb = _lds(m, n, k, layout)
-    for mode in (1, 2, 3):
-        ea, eb = orc.make_inputs(m, n, k, layout, mode)
-        a, b, c = _to_dev(torch, ea, eb, m, n, k, layout)
-        with bm.Gemm.from_tensors(a, b, c, layout) as g:
-            sched = g.schedule()
-            assert sched["k_split_clusters"] > 8, sched
-            for _ in range(2):
-                g.launch()
-            assert g.status() == (bm.BM_OK, 0)
-        want = orc.gemm_f32(k, layout, ea, lda, eb, ldb, 0, m, 0, n).astype(np.float16).view(np.uint16)
-        got = _bits(c)
-        assert np.array_equal(got, want), f"mode {mode} {sched}: " + _describe_mismatch(got, want, m, n, 128, 256)
-
-
-@pytest.mark.parametrize("layout", ["NT", "TN"])
-def test_k_split_skinny_baseline_shape(bm, orc, cuda, layout):
-    """BASELINE configs[3] (M=128, N=28672, K=8192), N(0, 0.02) inputs: the K
-    split over all SMs agrees with the whole-tile schedule within the
-    tolerance, with sampled FP64 oracle entries, and repeats bit for bit."""
-    torch = cuda
-    m, n, k = 128, 28672, 8192
-    a, b, c = bm.alloc_operands(m, n, k, layout, mode=5, seed=4)
-    c_whole = torch.empty_like(c)
-    _run(bm, a, b, c_whole, layout, bm.SPLIT_NONE, variant=0)
-    outs = []
-    with bm.Gemm.from_tensors(a, b, c, layout) as g:
-        sched = g.schedule()
-        assert sched["k_split_clusters"] == sched["resident_clusters"], sched
-        for _ in range(2):
-            c.fill_(float("nan"))
-            g.launch()
-            assert g.status() == (bm.BM_OK, 0)
-            outs.append(_bits(c).copy())
-    assert np.array_equal(outs[0], outs[1]), "K split must repeat bit for bit"
-    got = outs[0].view(np.float16).astype(np.float64)
-    want = c_whole.float().cpu().numpy().astype(np.float64)
-    lim = RTOL * np.abs(want) + ATOL * np.sqrt(k / 4096) + 2 ** -10 * np.abs(want)
-    assert np.all(np.abs(got - want) <= lim), "K split vs whole tiles"
-    rng = np.random.default_rng(8)
-    rows, cols = rng.integers(0, m, 2048), rng.integers(0, n, 2048)
-    ha, hb = _bits(a).reshape(-1), _bits(b).reshape(-1)
-    lda, ldb = _lds(m, n, k, layout)
-    ref = orc.entries_f64(k, layout, ha, lda, hb, ldb, rows, cols)
-    bad, merr, _ = orc.check(outs[0][cols, rows], ref, k, RTOL, ATOL)
-    assert bad == 0, f"{bad} bad samples, max err {merr}"
-
-
-def test_k_split_flag_wait_expires_and_reports(bm, cuda):
-    """Failure detection without a GPU fault: contributors withhold their
-    ready flags, each owner's bounded wait expires after 1 ms, the status word
-    reports it, the status call clears the flags, and the next launch on the
-    same handle is correct."""
-    torch = cuda
-    m, n, k = 128, 2048, 64 * 40
-    a, b, c = bm.alloc_operands(m, n, k, "TN", mode=1)
-    c.fill_(float("nan"))
-    with bm.Gemm.from_tensors(a, b, c, "TN") as g:
-        assert g.schedule()["k_split_clusters"] > 8
-        g.set_debug(1_000_000, bm.DEBUG_SPLIT_FLAGS_NEVER)
-        g.launch()
-        rc, bits = g.status()
-        assert rc == bm.BM_ERR_DEVICE_TIMEOUT
-        assert bits & (1 << 2), f"bits {bits:#x}"
-        g.set_debug(2_000_000_000, 0)
-        c.fill_(float("nan"))
-        g.launch()
-        assert g.status() == (bm.BM_OK, 0)
-    assert torch.all(c == float(k)).item()
