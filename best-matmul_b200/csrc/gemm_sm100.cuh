@@ -25,8 +25,12 @@
 //              is kBN * kNumN wide, so every A byte brought on chip feeds
 //              kNumN MMAs. kNumN = 2 with kBN = 256 fills all 512 TMEM columns.
 // With room for two accumulators in TMEM (kAccStages = 2) the epilogue of tile
-// i overlaps the mainloop of tile i+1; with one, the producer still prefetches
-// the next tile's first stages while the epilogue drains TMEM.
+// i overlaps the mainloop of tile i+1. With one (the 256x512 pair tile) the
+// epilogue reads the accumulator into packed FP16 registers and releases TMEM
+// before storing, first columns [0, 256) then [256, 512), and the MMA issuer
+// starts the next tile's first k-blocks on the half that is free first.
+// Tiles are scheduled by schedule.cuh (whole tiles in full waves; a half-empty
+// last wave in 256-column halves).
 //
 // Every wait is bounded (ptx::bm_wait); on expiry the CTA records an error
 // code in the device status word, tells its other roles to stop, drains its
